@@ -1,0 +1,126 @@
+/*
+ * wc_t5cuda.h — C ABI of the B200 (sm_100a) XTR-base T5 encoder backend.
+ *
+ * This is the boundary a `t5-cuda` feature of dropbox/witchcraft binds over
+ * FFI.  It replaces, behind the unchanged Embedder API, the encoder backend
+ * contract of the reference:
+ *   T5ModelBuilder::build_encoder   src/quantized_t5.rs:731-749
+ *   T5EncoderModel::load            src/quantized_t5.rs:680-696
+ *   T5EncoderModel::forward         src/quantized_t5.rs:698-701
+ *   T5EncoderModel::device          src/quantized_t5.rs:703-705
+ * (the OpenVINO backend implements the same surface, src/openvino_t5.rs:151-245).
+ *
+ * Conventions
+ *   - Every function returns 0 (WC_OK) on success or a negative WC_E* code.
+ *     Nothing aborts, throws or exits across this boundary.
+ *   - The caller owns all host buffers.  A handle owns its device memory,
+ *     stream and workspaces; wc_t5_destroy frees them.
+ *   - One handle drives one GPU.  A handle is not re-entrant (wrap it in a
+ *     mutex); different handles may be used from different threads at once.
+ *   - Kernels never trap: a failed in-kernel wait sets a device status word
+ *     that the forward call turns into WC_E_TIMEOUT.
+ *   - Functions taking `void* stream` accept a cudaStream_t (NULL = legacy
+ *     default stream) and device pointers; they return once the work is
+ *     enqueued.
+ */
+#ifndef WC_T5CUDA_H
+#define WC_T5CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  WC_OK = 0,
+  WC_E_INVALID_ARG = -1,   /* null pointer, bad size, token id >= vocab, ... */
+  WC_E_GGUF = -2,          /* malformed or truncated GGUF, missing tensor */
+  WC_E_UNSUPPORTED = -3,   /* tensor dtype/shape or config this backend does not run */
+  WC_E_CUDA = -4,          /* CUDA runtime error (no device, out of memory, launch failure) */
+  WC_E_TIMEOUT = -5,       /* an in-kernel wait hit its time limit */
+  WC_E_CONFIG = -6         /* config.json missing a field or unparsable */
+};
+
+typedef struct wc_t5 wc_t5;
+
+/* Number of CUDA devices visible to this process (0 when none; never fails). */
+int wc_t5_device_count(void);
+
+/* Build an encoder on device `device_ordinal` from the bytes of xtr.gguf and
+ * the text of config.json (T5ModelBuilder::load + build_encoder,
+ * src/quantized_t5.rs:713-749).  Q4_K tensors are uploaded unchanged (raw
+ * super-blocks); F32/F16 tensors are uploaded as f32.  On failure *out is set
+ * to NULL and the reason is available from wc_t5_last_error(NULL). */
+int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf_len, const char* config_json,
+                 wc_t5** out);
+
+/* Free everything the handle owns.  NULL is accepted. */
+int wc_t5_destroy(wc_t5* h);
+
+/* Last error message of the handle (or of the last failed wc_t5_create when
+ * h is NULL).  The string lives until the next call on the same handle. */
+const char* wc_t5_last_error(const wc_t5* h);
+
+/* Encode a padded batch (T5EncoderModel::forward, src/quantized_t5.rs:698-701,
+ * generalised from batch 1 to B rows with a key padding mask).
+ *   ids      host u32 [B][L], row-major; positions >= lengths[b] are ignored
+ *   lengths  host i32 [B], 1 <= lengths[b] <= L (NULL = every row has length L)
+ *   L        1..2048 (the Embedder's window, src/embedder.rs:27)
+ *   out      host f32 [B][L][128]: the raw 768->128 projection (what the
+ *            reference forward returns; rows past lengths[b] are 0)
+ *   norms    host f32 [B][L] L2 norm of each raw row, or NULL
+ *   out_normalised host f32 [B][L][128] rows divided by their norm, or NULL
+ * Each row b equals the reference's batch-1 forward of ids[b][0:lengths[b]].
+ * Blocks until the results are in host memory. */
+int wc_t5_forward(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, int L, float* out, float* norms,
+                  float* out_normalised);
+
+/* Same as wc_t5_forward with device buffers, enqueued on `stream`; returns
+ * without synchronising (the status word is checked by the next blocking
+ * call, or by wc_t5_sync). */
+int wc_t5_forward_device(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengths, int B, int L, float* d_out,
+                         float* d_norms, float* d_out_normalised, void* stream);
+
+/* Wait for the handle's work on `stream` and report any in-kernel failure. */
+int wc_t5_sync(wc_t5* h, void* stream);
+
+/* Model dimensions of a handle: d_model, number of layers, output dim, vocab. */
+int wc_t5_dims(const wc_t5* h, int* d_model, int* n_layers, int* d_proj, int* vocab);
+
+/* ---- kernel-level entry points (device pointers), used by the parity tests
+ *      and the microbenchmarks ---- */
+
+/* Q4_K super-blocks -> f32, bit-exact with the reference dequant (candle
+ * k_quants BlockQ4K as used at src/quantized_t5.rs:44). */
+int wc_q4k_dequant(const void* d_blocks, int64_t nblocks, float* d_out, void* stream);
+
+/* Y = X . W^T with X bf16 [M][K] and W Q4_K [N][K/256 blocks]
+ * (QMatMul::forward, src/quantized_t5.rs:39-49; QTiledOp, src/fused_matmul.rs:46-59).
+ * epilogue: 0 = bf16 out [M][N]; 1 = gated GELU: gelu_tanh(X.W^T) * (X.W_up^T)
+ *           as bf16 [M][N] (T5DenseGatedActDense, src/quantized_t5.rs:231-252;
+ *           QGatedMatMul, src/fused_matmul.rs:138-177), d_w_up required;
+ *           2 = f32 residual: out[M][N] += X.W^T (src/fast_ops.rs:42-48);
+ *           3 = f32 out [M][N].
+ * K % 256 == 0, N % 128 == 0, M >= 1. */
+int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const void* d_w_up, int N, int epilogue,
+                void* d_out, void* stream);
+
+/* Encoder self-attention (src/quantized_t5.rs:426-500) over a padded batch.
+ * d_qkv bf16 [B*L][3*H*64] (q | k | v), d_out bf16 [B*L][H*64], d_lengths
+ * i32 [B], d_bias_table f32 [num_buckets][H] (relative_attention_bias).
+ * No 1/sqrt(d) scaling; keys >= lengths[b] are masked. */
+int wc_attention(const void* d_qkv, int B, int L, int H, const int32_t* d_lengths, const float* d_bias_table,
+                 int num_buckets, int max_distance, void* d_out, void* stream);
+
+/* T5 bidirectional relative-position bucket of (query, key) as this backend
+ * computes it (host side; src/quantized_t5.rs:447-483).  Returns the bucket
+ * or WC_E_INVALID_ARG. */
+int wc_t5_relative_bucket(int query, int key, int num_buckets, int max_distance);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WC_T5CUDA_H */

@@ -1,0 +1,146 @@
+"""End-to-end parity of the CUDA encoder through the C ABI (wc_t5_forward)
+against the CPU oracle and the HF-pinned golden output.
+
+Tolerance (per token, on the L2-normalised 128-d output, which is what the
+Embedder returns): cosine >= 0.999 and max-abs <= 2e-2."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import oracle as O
+from witchcraft_b200._lib import WcError
+from witchcraft_b200.t5cuda import Embedder, T5EncoderModel
+
+from gpu_util import cosine_rows
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.999
+MAX_ABS = 2e-2
+
+
+def _normalise(v):
+    n = np.linalg.norm(v, axis=-1, keepdims=True)
+    return v / np.where(n > 0, n, 1)
+
+
+def _check(gpu_raw, ref_raw, lengths):
+    for b, n in enumerate(lengths):
+        g, r = gpu_raw[b, :n], ref_raw[b, :n]
+        cos = cosine_rows(g, r)
+        assert cos.min() >= COS_MIN, (b, cos.min())
+        assert np.abs(_normalise(g) - _normalise(r)).max() <= MAX_ABS, b
+        assert np.all(gpu_raw[b, n:] == 0)
+
+
+@pytest.fixture(scope="module")
+def tiny_gpu(tiny_model):
+    m = T5EncoderModel(tiny_model.gguf, tiny_model.config.to_json(), 0)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def xtr_gpu(xtr_model):
+    m = T5EncoderModel(xtr_model.gguf, xtr_model.config.to_json(), 0)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def xtr_oracle(xtr_model):
+    return O.OracleEncoder(xtr_model)
+
+
+def test_tiny_matches_hf_golden(tiny_gpu):
+    g = np.load(os.path.join(GOLDEN, "t5_tiny_golden.npz"))
+    out = tiny_gpu.forward(g["ids"], g["lengths"])
+    _check(out, g["out"], g["lengths"])
+
+
+def test_xtr_config1_shape_matches_oracle(xtr_gpu, xtr_oracle):
+    """Config 1 shape (L = 128, no padding) on 2 of its 16 rows, plus norms
+    and normalised outputs."""
+    ids = np.random.default_rng(1).integers(3, 32128, (2, 128)).astype(np.uint32)
+    raw, norms, outn = xtr_gpu.forward_full(ids)
+    ref = xtr_oracle.encode(ids)
+    _check(raw, ref, [128, 128])
+    np.testing.assert_allclose(norms, np.linalg.norm(raw, axis=-1), rtol=1e-5)
+    np.testing.assert_allclose(outn, _normalise(raw), atol=1e-6)
+
+
+def test_xtr_ragged_padded_batch(xtr_gpu, xtr_oracle):
+    rng = np.random.default_rng(6)
+    lengths = [300, 1, 64, 65, 129, 200]
+    L = 300
+    ids = rng.integers(3, 32128, (len(lengths), L)).astype(np.uint32)
+    out = xtr_gpu.forward(ids, lengths)
+    ref = xtr_oracle.encode(ids, lengths)
+    _check(out, ref, lengths)
+    # each row equals the unpadded single-sequence forward
+    for b in (1, 3):
+        single = xtr_gpu.forward(ids[b:b + 1, :lengths[b]])
+        cos = cosine_rows(single[0], out[b, :lengths[b]])
+        assert cos.min() > 0.9999
+
+
+def test_xtr_query_shapes(xtr_gpu, xtr_oracle):
+    """Config 5 shapes: 32-token padded queries, lengths U[4, 32]."""
+    rng = np.random.default_rng(6)
+    lengths = rng.integers(4, 33, 8).tolist()
+    ids = rng.integers(3, 32128, (8, 32)).astype(np.uint32)
+    _check(xtr_gpu.forward(ids, lengths), xtr_oracle.encode(ids, lengths), lengths)
+
+
+def test_long_window_tiny(tiny_gpu, tiny_model):
+    ids = np.random.default_rng(8).integers(3, 512, (1, 2048)).astype(np.uint32)
+    _check(tiny_gpu.forward(ids), O.OracleEncoder(tiny_model).encode(ids), [2048])
+
+
+def test_embedder_multi_window_tiny(tiny_gpu, tiny_model):
+    """Embedder over a 2600-token document: two overlapping windows summed,
+    min-norm filter, L2 (src/embedder.rs:22-102), CUDA vs oracle."""
+    ids = np.random.default_rng(9).integers(3, 512, 2600).astype(np.uint32)
+    got, offs = Embedder(tiny_gpu).embed_ids(ids)
+    orc = O.OracleEncoder(tiny_model)
+
+    class _OracleModel:
+        d_proj = 128
+
+        def forward(self, x, lengths=None):
+            return orc.encode(np.atleast_2d(x), lengths)
+    ref, roffs = Embedder(_OracleModel()).embed_ids(ids)
+    assert offs == roffs
+    assert cosine_rows(got[0], ref[0]).min() >= COS_MIN
+    assert np.abs(got - ref).max() <= MAX_ABS
+
+
+def test_embed_batch_matches_single(tiny_gpu):
+    rng = np.random.default_rng(10)
+    docs = [rng.integers(3, 512, n).astype(np.uint32) for n in (3, 40, 41, 300, 2100, 17)]
+    e = Embedder(tiny_gpu)
+    for (b, _), d in zip(e.embed_ids_batch(docs, max_batch_tokens=2048), docs):
+        s, _ = e.embed_ids(d)
+        assert cosine_rows(b[0], s[0]).min() > 0.9999
+
+
+def test_forward_rejects_bad_input(tiny_gpu):
+    with pytest.raises(WcError) as ei:
+        tiny_gpu.forward(np.array([[1, 2, 99999]], np.uint32))
+    assert ei.value.code == -1
+    with pytest.raises(WcError):
+        tiny_gpu.forward(np.zeros((2, 8), np.uint32), [8, 9])
+    with pytest.raises(WcError):
+        tiny_gpu.forward(np.zeros((1, 2049), np.uint32))
+
+
+def test_two_handles_on_one_device(tiny_model):
+    a = T5EncoderModel(tiny_model.gguf, tiny_model.config.to_json(), 0)
+    b = T5EncoderModel(tiny_model.gguf, tiny_model.config.to_json(), 0)
+    ids = np.random.default_rng(2).integers(3, 512, (2, 50)).astype(np.uint32)
+    np.testing.assert_array_equal(a.forward(ids), b.forward(ids))
+    a.close()
+    np.testing.assert_array_equal(b.forward(ids), b.forward(ids))
+    b.close()

@@ -1,0 +1,148 @@
+"""Kernel-level parity on the GPU through the C ABI: bit-exact Q4_K dequant,
+the tcgen05 Q4_K GEMM (all epilogues, config-2 shapes and ragged M) and the
+encoder attention (config-3 shape, padding, long sequences)."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import oracle as O
+from witchcraft_b200._lib import check, lib
+from witchcraft_b200.synth import quantize_q4k
+
+from gpu_util import dequant_gpu, dptr, gemm_gpu, stream_ptr
+
+pytestmark = pytest.mark.gpu
+
+
+def _same_bits(a, b):
+    a = np.asarray(a, np.float32).reshape(-1)
+    b = np.asarray(b, np.float32).reshape(-1)
+    both_nan = np.isnan(a) & np.isnan(b)
+    return np.all((a.view(np.uint32) == b.view(np.uint32)) | both_nan)
+
+
+def test_dequant_bit_exact_against_golden():
+    g = np.load(os.path.join(GOLDEN, "q4k_golden.npz"))
+    assert _same_bits(dequant_gpu(g["blocks"]).cpu().numpy(), g["values"])
+
+
+def test_dequant_bit_exact_full_embedding_table(xtr_model):
+    blocks = xtr_model.q4k["encoder.embed_tokens.weight"]
+    assert _same_bits(dequant_gpu(blocks).cpu().numpy(), O.q4k_dequant(blocks))
+
+
+def _gelu(g):
+    return 0.5 * g * (1.0 + torch.tanh(0.7978845608 * (g + 0.044715 * g ** 3)))
+
+
+def _weights(N, K, seed):
+    w = np.random.default_rng(seed).standard_normal((N, K)).astype(np.float32) * 0.02
+    blocks = quantize_q4k(w)
+    wd = torch.from_numpy(O.q4k_dequant_matrix(blocks)).cuda()
+    return blocks, wd
+
+
+@pytest.mark.parametrize("M,K,N", [(8192, 768, 2304), (8192, 2048, 768), (1, 768, 768), (77, 768, 2304),
+                                   (300, 2048, 768), (129, 256, 128), (2048, 768, 128)])
+@pytest.mark.parametrize("epi", [0, 3])
+def test_gemm_store(M, K, N, epi):
+    blocks, wd = _weights(N, K, seed=M + N)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(2)).cuda().to(torch.bfloat16)
+    y = gemm_gpu(x, blocks, epi).float()
+    # same bf16-rounded operands, fp32 accumulation
+    ref = x.float() @ wd.to(torch.bfloat16).float().T
+    tol = 2e-2 if epi == 0 else 2e-3
+    err = (y - ref).abs().max().item() / ref.abs().max().item()
+    assert err < tol, err
+    # and against the unrounded f32 weights (the reference's numbers)
+    ref32 = x.float() @ wd.T
+    assert ((y - ref32).abs().max() / ref32.abs().max()).item() < 3e-2
+
+
+@pytest.mark.parametrize("M,K,F", [(8192, 768, 2048), (200, 768, 2048), (64, 256, 512)])
+def test_gemm_geglu(M, K, F):
+    b0, w0 = _weights(F, K, 10)
+    b1, w1 = _weights(F, K, 11)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(3)).cuda().to(torch.bfloat16)
+    y = gemm_gpu(x, b0, 1, w_up_blocks=b1).float()
+    xf = x.float()
+    ref = _gelu(xf @ w0.to(torch.bfloat16).float().T) * (xf @ w1.to(torch.bfloat16).float().T)
+    err = ((y - ref).abs().max() / ref.abs().max()).item()
+    assert err < 2e-2, err
+
+
+def test_gemm_residual_accumulates():
+    M, K, N = 333, 2048, 768
+    blocks, wd = _weights(N, K, 12)
+    x = torch.randn(M, K).cuda().to(torch.bfloat16)
+    base = torch.randn(M, N, device="cuda")
+    out = base.clone()
+    gemm_gpu(x, blocks, 2, out=out)
+    ref = base + x.float() @ wd.to(torch.bfloat16).float().T
+    assert ((out - ref).abs().max() / ref.abs().max()).item() < 2e-3
+
+
+def test_gemm_rejects_bad_shapes():
+    l = lib()
+    x = torch.zeros(8, 300, dtype=torch.bfloat16, device="cuda")
+    assert l.wc_gemm_q4k(dptr(x), 8, 300, dptr(x), None, 128, 0, dptr(x), stream_ptr()) == -1
+    assert l.wc_gemm_q4k(dptr(x), 8, 256, dptr(x), None, 100, 0, dptr(x), stream_ptr()) == -1
+    assert l.wc_gemm_q4k(dptr(x), 8, 256, dptr(x), None, 128, 1, dptr(x), stream_ptr()) == -1
+
+
+def _attention_gpu(qkv_bf16, B, L, H, lengths, bias_tab):
+    out = torch.empty(B * L, H * 64, dtype=torch.bfloat16, device="cuda")
+    dl = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    db = torch.from_numpy(np.ascontiguousarray(bias_tab, np.float32)).cuda()
+    check(lib().wc_attention(dptr(qkv_bf16), B, L, H, dptr(dl), dptr(db), 32, 128, dptr(out), stream_ptr()))
+    torch.cuda.synchronize()
+    return out
+
+
+def _attention_torch(qkv, B, L, H, lengths, bias_tab):
+    """fp32 reference: softmax(QK^T + bias, key mask) V without scaling."""
+    q, k, v = qkv.float().view(B, L, 3, H, 64).unbind(2)
+    q, k, v = (t.permute(0, 2, 1, 3) for t in (q, k, v))
+    delta = torch.arange(L)[None, :] - torch.arange(L)[:, None]
+    lut = torch.tensor([O.bucket(0, d) if d >= 0 else O.bucket(-d, 0) for d in range(-(L - 1), L)])
+    bucket = lut[delta + L - 1].cuda()
+    bias = torch.from_numpy(bias_tab).cuda()[bucket].permute(2, 0, 1)  # H, L, L
+    s = q @ k.transpose(-1, -2) + bias[None]
+    mask = torch.arange(L, device="cuda")[None, :] >= torch.tensor(lengths, device="cuda")[:, None]
+    s = s.masked_fill(mask[:, None, None, :], float("-inf"))
+    o = torch.softmax(s, -1) @ v
+    return o.permute(0, 2, 1, 3).reshape(B * L, H * 64)
+
+
+@pytest.mark.parametrize("B,L,lengths", [(2, 128, [128, 128]), (4, 200, [200, 130, 64, 1]),
+                                         (2, 65, [65, 33]), (1, 2048, [2048]), (3, 1, [1, 1, 1])])
+def test_attention_matches_oracle(B, L, lengths):
+    H = 12
+    g = torch.Generator().manual_seed(B * 1000 + L)
+    qkv = torch.randn(B * L, 3 * H * 64, generator=g).to(torch.bfloat16)
+    bias_tab = (np.random.default_rng(L).standard_normal((32, H)) * 0.1).astype(np.float32)
+    out = _attention_gpu(qkv.cuda(), B, L, H, lengths, bias_tab).float().cpu().numpy()
+    ref = O.attention(qkv.float().numpy(), B, L, H, lengths, bias_tab)
+    for b in range(B):
+        rows = slice(b * L, b * L + lengths[b])
+        err = np.abs(out[rows] - ref[rows]).max()
+        assert err < 2e-2, (b, err)
+
+
+def test_attention_config3_against_torch():
+    """Config 3: B=64, L=512, 12 heads, lengths U[32, 512], bias N(0, 0.1)."""
+    B, L, H = 64, 512, 12
+    rng = np.random.default_rng(4)
+    lengths = rng.integers(32, 513, B).tolist()
+    qkv = torch.randn(B * L, 3 * H * 64, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+    bias_tab = (np.random.default_rng(3).standard_normal((32, H)) * 0.1).astype(np.float32)
+    out = _attention_gpu(qkv, B, L, H, lengths, bias_tab).float()
+    ref = _attention_torch(qkv, B, L, H, lengths, bias_tab)
+    for b in range(B):
+        rows = slice(b * L, b * L + lengths[b])
+        assert (out[rows] - ref[rows]).abs().max().item() < 2e-2, b
+        assert torch.all(torch.isfinite(out[b * L:(b + 1) * L]))

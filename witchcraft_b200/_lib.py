@@ -1,0 +1,71 @@
+"""ctypes binding of the native library (include/wc_t5cuda.h).
+
+The library is built in-tree by `witchcraft_b200.build`; loading fails loudly
+when it is missing.  There is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libwc_t5cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "wc_t5cuda.h")
+
+WC_OK = 0
+ERRORS = {-1: "WC_E_INVALID_ARG", -2: "WC_E_GGUF", -3: "WC_E_UNSUPPORTED", -4: "WC_E_CUDA",
+          -5: "WC_E_TIMEOUT", -6: "WC_E_CONFIG"}
+
+_lib = None
+
+c_void_p, c_int, c_int64, c_size_t = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+_P = ctypes.POINTER
+
+_SIGNATURES = {
+    "wc_t5_device_count": (c_int, []),
+    "wc_t5_create": (c_int, [c_int, c_void_p, c_size_t, ctypes.c_char_p, _P(c_void_p)]),
+    "wc_t5_destroy": (c_int, [c_void_p]),
+    "wc_t5_last_error": (ctypes.c_char_p, [c_void_p]),
+    "wc_t5_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "wc_t5_forward_device": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                     c_void_p]),
+    "wc_t5_sync": (c_int, [c_void_p, c_void_p]),
+    "wc_t5_dims": (c_int, [c_void_p, _P(c_int), _P(c_int), _P(c_int), _P(c_int)]),
+    "wc_q4k_dequant": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
+    "wc_gemm_q4k": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "wc_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "wc_t5_relative_bucket": (c_int, [c_int, c_int, c_int, c_int]),
+}
+
+
+class WcError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built; run `python -m witchcraft_b200.build`")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def header_symbols() -> list[str]:
+    """Function names declared in include/wc_t5cuda.h."""
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(wc_[a-z0-9_]+)\s*\(", txt)))
+
+
+def check(code: int, handle=None) -> None:
+    if code != WC_OK:
+        msg = lib().wc_t5_last_error(handle)
+        raise WcError(code, msg.decode() if msg else "")

@@ -1,0 +1,141 @@
+// Memory-bound kernels of the encoder: Q4_K dequant, embedding gather fused
+// with the first RMSNorm, and RMSNorm (T5LayerNorm, src/quantized_t5.rs:162-173:
+// f32 statistics, no mean subtraction, no bias, x / sqrt(var + eps) * w).
+// One warp per row, 16-byte vector accesses, the row kept in registers.
+#include "common.cuh"
+#include "elementwise.h"
+#include "q4k.cuh"
+
+namespace wc {
+
+namespace {
+
+constexpr int kMaxD = 1024;           // d_model supported by the row kernels
+constexpr int kPerLane = kMaxD / 32;  // floats per lane at kMaxD
+
+__global__ void q4k_dequant_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, float* __restrict__ out) {
+  // one thread per 8 outputs; 32 threads per super-block
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t blk = gid >> 5;
+  if (blk >= nblocks) return;
+  const int e = static_cast<int>(gid & 31) * 8;
+  const uint8_t* p = blocks + blk * 144;
+  const Q4KScales s = q4k_load_scales(p);
+  float v[8];
+  q4k_block_elems8(p, s, e, v);
+  float4* o = reinterpret_cast<float4*>(out + blk * 256 + e);
+  o[0] = make_float4(v[0], v[1], v[2], v[3]);
+  o[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// lane owns elements [8*(lane + 32*i), +8) for i < D/256
+__global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const uint32_t* __restrict__ ids,
+                                     const int32_t* __restrict__ lengths, int L, int M, int D,
+                                     const float* __restrict__ w, float eps, float* __restrict__ x,
+                                     __nv_bfloat16* __restrict__ xn) {
+  const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const int b = m / L, i = m - b * L;
+  const uint32_t id = i < lengths[b] ? ids[m] : 0u;
+  const int nb = D / 256;
+  const uint8_t* row = table + static_cast<size_t>(id) * nb * 144;
+  float v[kMaxD / 256][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxD / 256; ++c) {
+    if (c < nb) {
+      const uint8_t* blk = row + c * 144;
+      const Q4KScales s = q4k_load_scales(blk);
+      q4k_block_elems8(blk, s, lane * 8, v[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
+    }
+  }
+  ss = warp_sum(ss);
+  const float den = sqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+  for (int c = 0; c < kMaxD / 256; ++c) {
+    if (c < nb) {
+      const int e = c * 256 + lane * 8;
+      float* xo = x + static_cast<size_t>(m) * D + e;
+      reinterpret_cast<float4*>(xo)[0] = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+      reinterpret_cast<float4*>(xo)[1] = make_float4(v[c][4], v[c][5], v[c][6], v[c][7]);
+      const float4 w0 = reinterpret_cast<const float4*>(w + e)[0];
+      const float4 w1 = reinterpret_cast<const float4*>(w + e)[1];
+      uint4 o;
+      o.x = pack_bf16x2(v[c][0] / den * w0.x, v[c][1] / den * w0.y);
+      o.y = pack_bf16x2(v[c][2] / den * w0.z, v[c][3] / den * w0.w);
+      o.z = pack_bf16x2(v[c][4] / den * w1.x, v[c][5] / den * w1.y);
+      o.w = pack_bf16x2(v[c][6] / den * w1.z, v[c][7] / den * w1.w);
+      *reinterpret_cast<uint4*>(xn + static_cast<size_t>(m) * D + e) = o;
+    }
+  }
+}
+
+// lane owns float4 groups lane + 32*i, i < D/128
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               __nv_bfloat16* __restrict__ y, int M, int D, float eps) {
+  const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const int ng = D / 128;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * D);
+  float4 v[kMaxD / 128];
+  float ss = 0.f;
+#pragma unroll
+  for (int g = 0; g < kMaxD / 128; ++g) {
+    if (g < ng) {
+      v[g] = xr[lane + 32 * g];
+      ss += v[g].x * v[g].x + v[g].y * v[g].y + v[g].z * v[g].z + v[g].w * v[g].w;
+    }
+  }
+  ss = warp_sum(ss);
+  const float den = sqrtf(ss / static_cast<float>(D) + eps);
+  uint2* yr = reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * D);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int g = 0; g < kMaxD / 128; ++g) {
+    if (g < ng) {
+      const float4 ww = wr[lane + 32 * g];
+      uint2 o;
+      o.x = pack_bf16x2(v[g].x / den * ww.x, v[g].y / den * ww.y);
+      o.y = pack_bf16x2(v[g].z / den * ww.z, v[g].w / den * ww.w);
+      yr[lane + 32 * g] = o;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t q4k_dequant_launch(const uint8_t* blocks, int64_t nblocks, float* out, cudaStream_t st) {
+  if (nblocks <= 0) return cudaSuccess;
+  const int64_t threads = nblocks * 32;
+  const int bs = 256;
+  q4k_dequant_kernel<<<static_cast<unsigned>((threads + bs - 1) / bs), bs, 0, st>>>(blocks, nblocks, out);
+  return cudaGetLastError();
+}
+
+cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, const int32_t* lengths, int L, int M,
+                                 int D, const float* w, float eps, float* x, __nv_bfloat16* xn, cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  if (D % 256 != 0 || D > kMaxD) return cudaErrorInvalidValue;
+  embed_rmsnorm_kernel<<<(M + 7) / 8, 256, 0, st>>>(table, ids, lengths, L, M, D, w, eps, x, xn);
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_launch(const float* x, const float* w, __nv_bfloat16* y, int M, int D, float eps,
+                           cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  if (D % 128 != 0 || D > kMaxD) return cudaErrorInvalidValue;
+  rmsnorm_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, w, y, M, D, eps);
+  return cudaGetLastError();
+}
+
+}  // namespace wc

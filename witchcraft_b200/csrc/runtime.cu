@@ -1,0 +1,620 @@
+// The encoder handle behind include/wc_t5cuda.h: weight upload, workspaces,
+// TMA descriptors and the per-forward launch sequence.
+//
+// Forward (one padded batch of B sequences x L tokens, M = B*L rows):
+//   embed_rmsnorm      x = dequant(embedding rows), xn = RMSNorm_0(x)
+//   per layer l:
+//     gemm  kEpiBF16   qkv = xn . [Wq|Wk|Wv]^T                (bf16 [M][3*inner])
+//     attention        att = softmax(QK^T + bias, key mask) V (bf16 [M][inner])
+//     gemm  kEpiResid  x += att . Wo^T                        (f32)
+//     rmsnorm          xn = RMSNorm_ff(x)
+//     gemm  kEpiGeGLU  h = gelu(xn . Wi0^T) * (xn . Wi1^T)    (bf16 [M][d_ff])
+//     gemm  kEpiResid  x += h . Wwo^T
+//     rmsnorm          xn = RMSNorm_{next attn | final}(x)
+//   gemm  kEpiProj     out = xn . Wlin^T, norms, out / norm   (f32 [M][128])
+// following T5Stack::forward / T5Block::forward / T5EncoderModel::forward
+// (src/quantized_t5.rs:654-670, 598-628, 698-701).  The residual stream x
+// stays f32; GEMM operands are bf16 with f32 accumulation in TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/wc_t5cuda.h"
+#include <algorithm>
+
+#include "attention.h"
+#include "common.cuh"
+#include "elementwise.h"
+#include "gemm_q4k.h"
+#include "t5_host.h"
+
+namespace wc {
+
+namespace {
+
+constexpr int kMaxL = 2048;  // Embedder window (src/embedder.rs:27)
+
+thread_local std::string g_create_error;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 activation matrix [rows][K], box 64 x 128, 128-byte swizzle.
+bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {K * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// raw Q4_K matrix [rows][K/256 * 144 bytes], box 144 x box_rows, no swizzle.
+bool make_q4k_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K, uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const uint64_t row_bytes = K / 256 * 144;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {144, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct LayerW {
+  uint8_t *qkv, *o, *wi0, *wi1, *wo;
+  float *ln0, *ln1;
+  CUtensorMap tm_qkv, tm_o, tm_wi0, tm_wi1, tm_wo;
+};
+
+}  // namespace
+
+}  // namespace wc
+
+struct wc_t5 {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  wc::T5Config cfg;
+  int inner = 0, d_proj = 128;
+  int bn_qkv = 0, bn_o = 0, bn_wi = 0, bn_wo = 0;
+  uint8_t* arena = nullptr;  // all weights, one allocation
+  uint8_t* embed = nullptr;
+  uint8_t* proj = nullptr;
+  float* final_ln = nullptr;
+  float* rel_bias = nullptr;
+  wc::BucketThresholds bt{};
+  std::vector<wc::LayerW> layers;
+  CUtensorMap tm_proj;
+  // workspaces (capacity in rows)
+  int64_t cap_rows = 0;
+  int cap_b = 0;
+  uint8_t* ws = nullptr;
+  float* x = nullptr;
+  __nv_bfloat16 *xn = nullptr, *qkv = nullptr, *att = nullptr, *hbuf = nullptr;
+  CUtensorMap tm_xn, tm_att, tm_h;
+  // host-API staging
+  uint32_t* d_ids = nullptr;
+  int32_t* d_len = nullptr;
+  float *d_out = nullptr, *d_norms = nullptr, *d_outn = nullptr;
+  uint32_t* d_status = nullptr;
+  std::string err;
+};
+
+namespace wc {
+namespace {
+
+int fail(wc_t5* h, int code, const std::string& msg) {
+  if (h)
+    h->err = msg;
+  else
+    g_create_error = msg;
+  return code;
+}
+
+int cuda_fail(wc_t5* h, cudaError_t e, const char* what) {
+  return fail(h, WC_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void free_workspace(wc_t5* h) {
+  if (h->ws) cudaFree(h->ws);
+  h->ws = nullptr;
+  h->cap_rows = 0;
+  h->cap_b = 0;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+int ensure_workspace(wc_t5* h, int64_t rows, int B) {
+  if (rows <= h->cap_rows && B <= h->cap_b) return WC_OK;
+  const int64_t cap = std::max<int64_t>((rows + 127) / 128 * 128, h->cap_rows);
+  const int capb = std::max(B, h->cap_b);
+  free_workspace(h);
+  const int D = h->cfg.d_model, F = h->cfg.d_ff, I = h->inner, P = h->d_proj;
+  size_t off = 0;
+  const size_t o_x = off; off = align256(off + cap * D * 4);
+  const size_t o_xn = off; off = align256(off + cap * D * 2);
+  const size_t o_qkv = off; off = align256(off + cap * 3 * I * 2);
+  const size_t o_att = off; off = align256(off + cap * I * 2);
+  const size_t o_h = off; off = align256(off + cap * F * 2);
+  const size_t o_ids = off; off = align256(off + cap * 4);
+  const size_t o_len = off; off = align256(off + capb * 4);
+  const size_t o_out = off; off = align256(off + cap * P * 4);
+  const size_t o_norms = off; off = align256(off + cap * 4);
+  const size_t o_outn = off; off = align256(off + cap * P * 4);
+  cudaError_t e = cudaMalloc(&h->ws, off);
+  if (e != cudaSuccess) {
+    h->ws = nullptr;
+    return cuda_fail(h, e, "workspace allocation");
+  }
+  h->x = reinterpret_cast<float*>(h->ws + o_x);
+  h->xn = reinterpret_cast<__nv_bfloat16*>(h->ws + o_xn);
+  h->qkv = reinterpret_cast<__nv_bfloat16*>(h->ws + o_qkv);
+  h->att = reinterpret_cast<__nv_bfloat16*>(h->ws + o_att);
+  h->hbuf = reinterpret_cast<__nv_bfloat16*>(h->ws + o_h);
+  h->d_ids = reinterpret_cast<uint32_t*>(h->ws + o_ids);
+  h->d_len = reinterpret_cast<int32_t*>(h->ws + o_len);
+  h->d_out = reinterpret_cast<float*>(h->ws + o_out);
+  h->d_norms = reinterpret_cast<float*>(h->ws + o_norms);
+  h->d_outn = reinterpret_cast<float*>(h->ws + o_outn);
+  if (!make_act_map(&h->tm_xn, h->xn, cap, D) || !make_act_map(&h->tm_att, h->att, cap, I) ||
+      !make_act_map(&h->tm_h, h->hbuf, cap, F))
+    return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
+  h->cap_rows = cap;
+  h->cap_b = capb;
+  return WC_OK;
+}
+
+int gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, int M,
+         int N, int K, void* out, int ldo, cudaStream_t st, float* norms = nullptr, float* outn = nullptr,
+         const int32_t* lengths = nullptr, int L = 0) {
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out = out;
+  p.ldo = ldo;
+  p.norms = norms;
+  p.out_normalised = outn;
+  p.lengths = lengths;
+  p.L = L;
+  p.status = h->d_status;
+  cudaError_t e = gemm_q4k_launch(epi, bn, a, w0, w1, p, st);
+  return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
+}
+
+int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, int L, float* out, float* norms,
+                   float* outn, cudaStream_t st) {
+  const T5Config& c = h->cfg;
+  const int D = c.d_model, F = c.d_ff, I = h->inner, H = c.num_heads;
+  const int M = B * L;
+  cudaError_t e;
+  if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, h->x, h->xn, st)) !=
+      cudaSuccess)
+    return cuda_fail(h, e, "embedding launch");
+  int rc;
+  for (int l = 0; l < c.num_layers; ++l) {
+    LayerW& w = h->layers[l];
+    if ((rc = gemm(h, kEpiBF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, M, 3 * I, D, h->qkv, 3 * I, st)))
+      return rc;
+    if ((e = attention_launch(h->qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
+      return cuda_fail(h, e, "attention launch");
+    if ((rc = gemm(h, kEpiResid, h->bn_o, h->tm_att, w.tm_o, w.tm_o, M, D, I, h->x, D, st))) return rc;
+    if ((e = rmsnorm_launch(h->x, w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
+      return cuda_fail(h, e, "rmsnorm launch");
+    if ((rc = gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, M, 2 * F, D, h->hbuf, F, st))) return rc;
+    if ((rc = gemm(h, kEpiResid, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, M, D, F, h->x, D, st))) return rc;
+    const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
+    if ((e = rmsnorm_launch(h->x, next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
+      return cuda_fail(h, e, "rmsnorm launch");
+  }
+  return gemm(h, kEpiProj, 128, h->tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
+              lengths, L);
+}
+
+int check_status(wc_t5* h, cudaStream_t st) {
+  uint32_t s = 0;
+  cudaError_t e = cudaMemcpyAsync(&s, h->d_status, 4, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(h, e, "synchronising the forward");
+  if (s & kStatusWaitTimeout) return fail(h, WC_E_TIMEOUT, "an in-kernel wait timed out");
+  if (s) return fail(h, WC_E_CUDA, "kernel reported status " + std::to_string(s));
+  return WC_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+}  // namespace wc
+
+using namespace wc;
+
+extern "C" int wc_t5_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+extern "C" const char* wc_t5_last_error(const wc_t5* h) { return h ? h->err.c_str() : g_create_error.c_str(); }
+
+extern "C" int wc_t5_destroy(wc_t5* h) {
+  if (!h) return WC_OK;
+  {
+    DeviceGuard g(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    free_workspace(h);
+    if (h->arena) cudaFree(h->arena);
+    if (h->d_status) cudaFree(h->d_status);
+    if (h->stream) cudaStreamDestroy(h->stream);
+  }
+  delete h;
+  return WC_OK;
+}
+
+extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf_len, const char* config_json,
+                            wc_t5** out) {
+  if (!out) return fail(nullptr, WC_E_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  T5Config cfg;
+  std::string err;
+  if (!config_parse(config_json, &cfg, &err)) return fail(nullptr, WC_E_CONFIG, err);
+  if (!cfg.gated_gelu)
+    return fail(nullptr, WC_E_UNSUPPORTED, "only the gated-gelu feed-forward (XTR / T5 v1.1) is supported");
+  if (cfg.d_kv != 64) return fail(nullptr, WC_E_UNSUPPORTED, "d_kv must be 64");
+  if (cfg.d_model % 256 || cfg.d_model > 1024 || cfg.d_ff % 256 || (cfg.num_heads * 64) % 256 ||
+      cfg.num_layers < 1 || cfg.num_buckets < 2 || cfg.num_buckets > 64 || cfg.vocab_size < 1)
+    return fail(nullptr, WC_E_UNSUPPORTED, "unsupported model dimensions in config.json");
+  std::unordered_map<std::string, GgufTensor> t;
+  if (!gguf_parse(gguf, gguf_len, &t, &err)) return fail(nullptr, WC_E_GGUF, err);
+
+  const int D = cfg.d_model, F = cfg.d_ff, I = cfg.num_heads * 64;
+  auto get = [&](const std::string& name, uint64_t rows, uint64_t cols, bool q4k, const GgufTensor** o) -> int {
+    auto it = t.find(name);
+    if (it == t.end()) return fail(nullptr, WC_E_GGUF, "GGUF has no tensor " + name);
+    const GgufTensor& g = it->second;
+    if (g.rows() != rows || g.cols() != cols || g.dims.size() > 2)
+      return fail(nullptr, WC_E_UNSUPPORTED,
+                  "tensor " + name + " has shape [" + std::to_string(g.rows()) + ", " + std::to_string(g.cols()) +
+                      "], expected [" + std::to_string(rows) + ", " + std::to_string(cols) + "]");
+    if (q4k && g.type != kGgmlQ4K) return fail(nullptr, WC_E_UNSUPPORTED, "tensor " + name + " is not Q4_K");
+    if (!q4k && g.type != kGgmlF32 && g.type != kGgmlF16)
+      return fail(nullptr, WC_E_UNSUPPORTED, "tensor " + name + " is not F32/F16");
+    *o = &g;
+    return WC_OK;
+  };
+  // the shared embedding: shared.weight, else encoder.embed_tokens.weight (src/quantized_t5.rs:682-687)
+  const char* emb_name = t.count("shared.weight") ? "shared.weight" : "encoder.embed_tokens.weight";
+  const GgufTensor *g_emb, *g_proj, *g_fln, *g_bias;
+  int rc;
+  if ((rc = get(emb_name, cfg.vocab_size, D, true, &g_emb))) return rc;
+  auto it_proj = t.find("linear.weight");
+  if (it_proj == t.end()) return fail(nullptr, WC_E_GGUF, "GGUF has no tensor linear.weight");
+  if ((rc = get("linear.weight", 128, D, true, &g_proj))) return rc;
+  if ((rc = get("encoder.final_layer_norm.weight", 1, D, false, &g_fln))) return rc;
+  if ((rc = get("encoder.block.0.layer.0.SelfAttention.relative_attention_bias.weight", cfg.num_buckets,
+                cfg.num_heads, false, &g_bias)))
+    return rc;
+  struct LT {
+    const GgufTensor *q, *k, *v, *o, *wi0, *wi1, *wo, *ln0, *ln1;
+  };
+  std::vector<LT> lt(cfg.num_layers);
+  for (int l = 0; l < cfg.num_layers; ++l) {
+    const std::string p = "encoder.block." + std::to_string(l) + ".layer.";
+    if ((rc = get(p + "0.SelfAttention.q.weight", I, D, true, &lt[l].q)) ||
+        (rc = get(p + "0.SelfAttention.k.weight", I, D, true, &lt[l].k)) ||
+        (rc = get(p + "0.SelfAttention.v.weight", I, D, true, &lt[l].v)) ||
+        (rc = get(p + "0.SelfAttention.o.weight", D, I, true, &lt[l].o)) ||
+        (rc = get(p + "0.layer_norm.weight", 1, D, false, &lt[l].ln0)) ||
+        (rc = get(p + "1.DenseReluDense.wi_0.weight", F, D, true, &lt[l].wi0)) ||
+        (rc = get(p + "1.DenseReluDense.wi_1.weight", F, D, true, &lt[l].wi1)) ||
+        (rc = get(p + "1.DenseReluDense.wo.weight", D, F, true, &lt[l].wo)) ||
+        (rc = get(p + "1.layer_norm.weight", 1, D, false, &lt[l].ln1)))
+      return rc;
+  }
+
+  int ndev = wc_t5_device_count();
+  if (device_ordinal < 0 || device_ordinal >= ndev)
+    return fail(nullptr, WC_E_CUDA,
+                "CUDA device " + std::to_string(device_ordinal) + " not available (" + std::to_string(ndev) +
+                    " visible)");
+  if (!get_encode_fn()) return fail(nullptr, WC_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+
+  wc_t5* h = new wc_t5();
+  h->device = device_ordinal;
+  h->cfg = cfg;
+  h->inner = I;
+  DeviceGuard guard(device_ordinal);
+  cudaError_t e;
+  int dmaj = 0;
+  cudaDeviceGetAttribute(&dmaj, cudaDevAttrComputeCapabilityMajor, device_ordinal);
+  if (dmaj != 10) {
+    delete h;
+    return fail(nullptr, WC_E_UNSUPPORTED, "this backend is built for sm_100a (B200); device has compute capability major " + std::to_string(dmaj));
+  }
+  if ((e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+      (e = cudaMalloc(&h->d_status, 4)) != cudaSuccess) {
+    std::string m = std::string("stream/status allocation: ") + cudaGetErrorString(e);
+    wc_t5_destroy(h);
+    return fail(nullptr, WC_E_CUDA, m);
+  }
+  cudaMemset(h->d_status, 0, 4);
+
+  // ---- weight arena layout
+  const size_t row_q4k_D = D / 256 * 144, row_q4k_F = F / 256 * 144, row_q4k_I = I / 256 * 144;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t o_emb = take(g_emb->nbytes);
+  const size_t o_proj = take(g_proj->nbytes);
+  const size_t o_fln = take(D * 4);
+  const size_t o_bias = take(cfg.num_buckets * cfg.num_heads * 4);
+  struct LO {
+    size_t qkv, o, wi0, wi1, wo, ln0, ln1;
+  };
+  std::vector<LO> lo(cfg.num_layers);
+  for (int l = 0; l < cfg.num_layers; ++l) {
+    lo[l].qkv = take(3 * I * row_q4k_D);
+    lo[l].o = take(D * row_q4k_I);
+    lo[l].wi0 = take(F * row_q4k_D);
+    lo[l].wi1 = take(F * row_q4k_D);
+    lo[l].wo = take(D * row_q4k_F);
+    lo[l].ln0 = take(D * 4);
+    lo[l].ln1 = take(D * 4);
+  }
+  std::vector<uint8_t> host(off, 0);
+  auto put_f32 = [&](size_t o, const GgufTensor* g) {
+    float* dst = reinterpret_cast<float*>(host.data() + o);
+    const size_t n = g->rows() * g->cols();
+    if (g->type == kGgmlF32) {
+      memcpy(dst, g->data, n * 4);
+    } else {  // F16 -> F32
+      for (size_t i = 0; i < n; ++i) {
+        uint16_t hb;
+        memcpy(&hb, g->data + 2 * i, 2);
+        __half_raw hr;
+        hr.x = hb;
+        dst[i] = __half2float(__half(hr));
+      }
+    }
+  };
+  memcpy(host.data() + o_emb, g_emb->data, g_emb->nbytes);
+  memcpy(host.data() + o_proj, g_proj->data, g_proj->nbytes);
+  put_f32(o_fln, g_fln);
+  put_f32(o_bias, g_bias);
+  for (int l = 0; l < cfg.num_layers; ++l) {
+    // q | k | v rows concatenated: raw super-blocks copied unchanged
+    memcpy(host.data() + lo[l].qkv, lt[l].q->data, lt[l].q->nbytes);
+    memcpy(host.data() + lo[l].qkv + lt[l].q->nbytes, lt[l].k->data, lt[l].k->nbytes);
+    memcpy(host.data() + lo[l].qkv + 2 * lt[l].q->nbytes, lt[l].v->data, lt[l].v->nbytes);
+    memcpy(host.data() + lo[l].o, lt[l].o->data, lt[l].o->nbytes);
+    memcpy(host.data() + lo[l].wi0, lt[l].wi0->data, lt[l].wi0->nbytes);
+    memcpy(host.data() + lo[l].wi1, lt[l].wi1->data, lt[l].wi1->nbytes);
+    memcpy(host.data() + lo[l].wo, lt[l].wo->data, lt[l].wo->nbytes);
+    put_f32(lo[l].ln0, lt[l].ln0);
+    put_f32(lo[l].ln1, lt[l].ln1);
+  }
+  if ((e = cudaMalloc(&h->arena, off)) != cudaSuccess ||
+      (e = cudaMemcpy(h->arena, host.data(), off, cudaMemcpyHostToDevice)) != cudaSuccess) {
+    std::string m = std::string("weight upload: ") + cudaGetErrorString(e);
+    wc_t5_destroy(h);
+    return fail(nullptr, WC_E_CUDA, m);
+  }
+  h->embed = h->arena + o_emb;
+  h->proj = h->arena + o_proj;
+  h->final_ln = reinterpret_cast<float*>(h->arena + o_fln);
+  h->rel_bias = reinterpret_cast<float*>(h->arena + o_bias);
+  h->bt = t5_bucket_thresholds(cfg.num_buckets, cfg.max_distance, kMaxL);
+  h->bn_qkv = gemm_q4k_bn_for(kEpiBF16, 3 * I);
+  h->bn_o = gemm_q4k_bn_for(kEpiResid, D);
+  h->bn_wi = gemm_q4k_bn_for(kEpiGeGLU, 2 * F);
+  h->bn_wo = gemm_q4k_bn_for(kEpiResid, D);
+  if (h->bn_qkv < 0 || h->bn_o < 0 || h->bn_wi < 0 || h->bn_wo < 0) {
+    wc_t5_destroy(h);
+    return fail(nullptr, WC_E_UNSUPPORTED, "no GEMM tiling for these model dimensions");
+  }
+  bool ok = make_q4k_map(&h->tm_proj, h->proj, 128, D, 128);
+  h->layers.resize(cfg.num_layers);
+  for (int l = 0; l < cfg.num_layers && ok; ++l) {
+    LayerW& w = h->layers[l];
+    w.qkv = h->arena + lo[l].qkv;
+    w.o = h->arena + lo[l].o;
+    w.wi0 = h->arena + lo[l].wi0;
+    w.wi1 = h->arena + lo[l].wi1;
+    w.wo = h->arena + lo[l].wo;
+    w.ln0 = reinterpret_cast<float*>(h->arena + lo[l].ln0);
+    w.ln1 = reinterpret_cast<float*>(h->arena + lo[l].ln1);
+    ok = make_q4k_map(&w.tm_qkv, w.qkv, 3 * I, D, gemm_q4k_w_box_rows(kEpiBF16, h->bn_qkv)) &&
+         make_q4k_map(&w.tm_o, w.o, D, I, gemm_q4k_w_box_rows(kEpiResid, h->bn_o)) &&
+         make_q4k_map(&w.tm_wi0, w.wi0, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
+         make_q4k_map(&w.tm_wi1, w.wi1, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
+         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiResid, h->bn_wo));
+  }
+  if (!ok) {
+    wc_t5_destroy(h);
+    return fail(nullptr, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a weight tensor");
+  }
+  *out = h;
+  return WC_OK;
+}
+
+extern "C" int wc_t5_dims(const wc_t5* h, int* d_model, int* n_layers, int* d_proj, int* vocab) {
+  if (!h) return WC_E_INVALID_ARG;
+  if (d_model) *d_model = h->cfg.d_model;
+  if (n_layers) *n_layers = h->cfg.num_layers;
+  if (d_proj) *d_proj = h->d_proj;
+  if (vocab) *vocab = h->cfg.vocab_size;
+  return WC_OK;
+}
+
+extern "C" int wc_t5_forward_device(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengths, int B, int L,
+                                    float* d_out, float* d_norms, float* d_outn, void* stream) {
+  if (!h) return WC_E_INVALID_ARG;
+  if (!d_ids || !d_lengths || !d_out || B < 1 || L < 1 || L > kMaxL || static_cast<int64_t>(B) * L > (1 << 26))
+    return fail(h, WC_E_INVALID_ARG, "invalid ids/lengths/out pointer or B, L out of range (1 <= L <= 2048)");
+  DeviceGuard g(h->device);
+  int rc = ensure_workspace(h, static_cast<int64_t>(B) * L, B);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(h->d_status, 0, 4, st);
+  if (e != cudaSuccess) return cuda_fail(h, e, "status reset");
+  return forward_device(h, d_ids, d_lengths, B, L, d_out, d_norms, d_outn, st);
+}
+
+extern "C" int wc_t5_sync(wc_t5* h, void* stream) {
+  if (!h) return WC_E_INVALID_ARG;
+  DeviceGuard g(h->device);
+  return check_status(h, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int wc_t5_forward(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, int L, float* out,
+                             float* norms, float* out_normalised) {
+  if (!h) return WC_E_INVALID_ARG;
+  if (!ids || !out || B < 1 || L < 1 || L > kMaxL || static_cast<int64_t>(B) * L > (1 << 26))
+    return fail(h, WC_E_INVALID_ARG, "invalid ids/out pointer or B, L out of range (1 <= L <= 2048)");
+  std::vector<int32_t> len(B, L);
+  if (lengths) {
+    for (int b = 0; b < B; ++b) {
+      if (lengths[b] < 1 || lengths[b] > L)
+        return fail(h, WC_E_INVALID_ARG, "lengths[" + std::to_string(b) + "] is outside [1, L]");
+      len[b] = lengths[b];
+    }
+  }
+  for (int b = 0; b < B; ++b)
+    for (int i = 0; i < len[b]; ++i)
+      if (ids[static_cast<size_t>(b) * L + i] >= static_cast<uint32_t>(h->cfg.vocab_size))
+        return fail(h, WC_E_INVALID_ARG, "token id " + std::to_string(ids[static_cast<size_t>(b) * L + i]) +
+                                             " is not below vocab_size " + std::to_string(h->cfg.vocab_size));
+  DeviceGuard g(h->device);
+  const int64_t M = static_cast<int64_t>(B) * L;
+  int rc = ensure_workspace(h, M, B);
+  if (rc) return rc;
+  cudaStream_t st = h->stream;
+  cudaError_t e;
+  if ((e = cudaMemsetAsync(h->d_status, 0, 4, st)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(h->d_ids, ids, M * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(h->d_len, len.data(), B * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+    return cuda_fail(h, e, "input upload");
+  rc = forward_device(h, h->d_ids, h->d_len, B, L, h->d_out, norms ? h->d_norms : nullptr,
+                      out_normalised ? h->d_outn : nullptr, st);
+  if (rc) return rc;
+  const size_t ob = static_cast<size_t>(M) * h->d_proj * 4;
+  if ((e = cudaMemcpyAsync(out, h->d_out, ob, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+      (norms && (e = cudaMemcpyAsync(norms, h->d_norms, M * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess) ||
+      (out_normalised &&
+       (e = cudaMemcpyAsync(out_normalised, h->d_outn, ob, cudaMemcpyDeviceToHost, st)) != cudaSuccess))
+    return cuda_fail(h, e, "output download");
+  return check_status(h, st);
+}
+
+// ---------------------------------------------------------------- kernel-level entry points
+
+namespace {
+uint32_t* kernel_status_word() {
+  // One status word per device for the kernel-level entry points.
+  static uint32_t* words[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!words[dev]) {
+    if (cudaMalloc(&words[dev], 4) != cudaSuccess) return nullptr;
+    cudaMemset(words[dev], 0, 4);
+  }
+  return words[dev];
+}
+}  // namespace
+
+extern "C" int wc_q4k_dequant(const void* d_blocks, int64_t nblocks, float* d_out, void* stream) {
+  if (nblocks < 0 || (nblocks > 0 && (!d_blocks || !d_out))) return WC_E_INVALID_ARG;
+  return q4k_dequant_launch(static_cast<const uint8_t*>(d_blocks), nblocks, d_out,
+                            static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? WC_OK
+             : WC_E_CUDA;
+}
+
+extern "C" int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const void* d_w_up, int N, int epilogue,
+                           void* d_out, void* stream) {
+  if (!d_x || !d_w || !d_out || M < 1 || K < 256 || K % 256 || N < 128 || N % 128) return WC_E_INVALID_ARG;
+  if (epilogue < 0 || epilogue > 3) return WC_E_INVALID_ARG;
+  if (epilogue == kEpiGeGLU && !d_w_up) return WC_E_INVALID_ARG;
+  const int tile_n = epilogue == kEpiGeGLU ? 2 * N : N;
+  const int bn = gemm_q4k_bn_for(epilogue, tile_n);
+  if (bn < 0) return WC_E_UNSUPPORTED;
+  const int box = gemm_q4k_w_box_rows(epilogue, bn);
+  CUtensorMap ta, tw0, tw1;
+  if (!make_act_map(&ta, d_x, M, K) || !make_q4k_map(&tw0, d_w, N, K, box) ||
+      !make_q4k_map(&tw1, epilogue == kEpiGeGLU ? d_w_up : d_w, N, K, box))
+    return WC_E_CUDA;
+  GemmParams p{};
+  p.M = M;
+  p.N = tile_n;
+  p.K = K;
+  p.out = d_out;
+  p.ldo = N;
+  p.status = kernel_status_word();
+  if (!p.status) return WC_E_CUDA;
+  return gemm_q4k_launch(epilogue, bn, ta, tw0, tw1, p, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? WC_OK
+             : WC_E_CUDA;
+}
+
+extern "C" int wc_attention(const void* d_qkv, int B, int L, int H, const int32_t* d_lengths,
+                            const float* d_bias_table, int num_buckets, int max_distance, void* d_out,
+                            void* stream) {
+  if (!d_qkv || !d_lengths || !d_bias_table || !d_out || B < 1 || L < 1 || L > kMaxL || H < 1 ||
+      num_buckets < 2 || num_buckets > 64 || max_distance < 1)
+    return WC_E_INVALID_ARG;
+  const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
+  return attention_launch(static_cast<const __nv_bfloat16*>(d_qkv), static_cast<__nv_bfloat16*>(d_out), d_lengths,
+                          B, L, H, d_bias_table, bt, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? WC_OK
+             : WC_E_CUDA;
+}
+
+extern "C" int wc_t5_relative_bucket(int query, int key, int num_buckets, int max_distance) {
+  if (num_buckets < 2 || num_buckets > 64 || max_distance < 1 || query < 0 || key < 0 || query >= kMaxL ||
+      key >= kMaxL)
+    return WC_E_INVALID_ARG;
+  const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
+  return t5_bucket_from_thresholds(bt, key - query);
+}
