@@ -1,0 +1,437 @@
+"""Encoder throughput benchmark (bulk document embedding).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the config-4 corpus, 131,072 synthetic documents with token counts
+clip(round(exp(N(5.0, 0.7))), 16, 512) (seed 5), sorted by length and packed
+into padded batches of <= 16,384 tokens.  One step = every rank encodes
+`--batches-per-step` of those batches (a seeded sample per rank, the same
+count on every rank: weak scaling), through the full 12-layer XTR-base
+encoder (random-init N(0, 0.02) weights quantized to Q4_K; synthetic ids).
+The metric is valid (unpadded) encoder tokens per second over all ranks.
+
+  value  device-resident inputs, kernel time of the K steps (CUDA events on
+         the launching stream, barrier + synchronize on both sides, max over
+         ranks)
+  e2e    the public C ABI call wc_t5_forward with pinned host buffers: the
+         H2D copy of ids/lengths and the D2H copy of the raw [B,L,128]
+         projection and norms are inside the timed region
+Multi-GPU: one process per GPU (torchrun), each rank a replica with its own
+batches; no collective on the data path (NCCL only for the barrier and the
+max-over-ranks of the timings).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "encoder tokens/sec XTR-base Q4_K (bulk embedding, config 4)"
+UNIT = "tokens/s"
+MAX_BATCH_TOKENS = 16384
+LAUNCHES_PER_FORWARD_PER_LAYER = 7   # qkv gemm, attention, o gemm, rmsnorm, wi gemm, wo gemm, rmsnorm
+# dram read+write bytes per launch of the dominant kernel from the committed ncu
+# capture (profiles/gemm_geglu_m16384.md); None until a capture exists.
+NCU_TRAFFIC_BYTES = None
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained"), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        def run():
+            q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            while not self._stop.is_set():
+                try:
+                    r = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                        "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                    vals = [v.strip() for v in r.stdout.strip().split(",")]
+                    if len(vals) == 6:
+                        self.rows.append(vals)
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[2 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _plan(world: int, rank: int, per_step: int, total_steps: int, seed: int = 17):
+    from witchcraft_b200 import shard
+    lengths = shard.config4_lengths()
+    batches = shard.plan_batches(lengths, MAX_BATCH_TOKENS)
+    rng = np.random.default_rng(seed)
+    order = rng.permutation(len(batches))
+    need = per_step * total_steps
+    # rank r walks its own disjoint slice of a seeded permutation of the corpus
+    mine = [batches[order[(rank * need + i) % len(batches)]] for i in range(need)]
+    return lengths, mine
+
+
+def _make_inputs(lengths, batch, rng):
+    B, L = len(batch.docs), batch.L
+    ids = np.zeros((B, L), np.uint32)
+    lens = lengths[batch.docs].astype(np.int32)
+    for b, n in enumerate(lens):
+        ids[b, :n] = rng.integers(3, 32128, n)
+    return ids, lens
+
+
+def cpu_reference_leg(model, lengths, target_s: float = 12.0, seed: int = 23):
+    """Times the CPU oracle (restatement of the reference's f32 CPU encoder)
+    on a bounded sample of config-4 documents with all host threads."""
+    from oracle import oracle as O
+    enc = O.OracleEncoder(model)
+    rng = np.random.default_rng(seed)
+    docs = rng.choice(len(lengths), 64, replace=False)
+    toks = 0
+    t0 = time.perf_counter()
+    n_docs = 0
+    for d in docs:
+        n = int(lengths[d])
+        ids = rng.integers(3, 32128, (1, n)).astype(np.uint32)
+        enc.encode(ids)
+        toks += n
+        n_docs += 1
+        if time.perf_counter() - t0 > target_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": toks / dt, "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+            "sample": f"{n_docs} config-4 documents ({toks} tokens) encoded one at a time (batch-1, as the "
+                      f"reference embeds), f32, oracle/oracle.c with OpenMP"}
+
+
+def run_reference(args):
+    world, rank, local = _dist_env()
+    if rank != 0:
+        return
+    from witchcraft_b200 import shard
+    from witchcraft_b200.synth import make_synthetic_model
+    model = make_synthetic_model(seed=0)
+    lengths = shard.config4_lengths()
+    vals = []
+    leg = None
+    for i in range(args.warmup + args.steps):
+        leg = cpu_reference_leg(model, lengths, target_s=args.ref_seconds, seed=100 + i)
+        if i >= args.warmup:
+            vals.append(leg["value"])
+    v = float(np.mean(vals))
+    leg["value"] = v
+    print(json.dumps({
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config 4 bulk embedding (131,072 docs, lengths lognormal(5.0,0.7) clip [16,512]); "
+                               "reference CPU arm: bounded document sample per step",
+                   "model": "XTR-base Q4_K random-init", "parallelism": "cpu threads"},
+        "cpu_baseline": leg,
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args):
+    import torch
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from witchcraft_b200._lib import check, lib
+    from witchcraft_b200.synth import make_synthetic_model
+    from witchcraft_b200.t5cuda import T5EncoderModel
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t)
+        return float(t.item())
+
+    model = make_synthetic_model(seed=0)
+    enc = T5EncoderModel(model.gguf, model.config.to_json(), device=local)
+    n_layers = model.config.num_layers
+    per_step = args.batches_per_step
+    lengths, mine = _plan(world, rank, per_step, args.warmup + args.steps)
+    rng = np.random.default_rng(1000 + rank)
+    host_inputs = [_make_inputs(lengths, b, rng) for b in mine]
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    # device-resident inputs and outputs
+    dev = []
+    max_rows = max(b.padded_tokens for b in mine)
+    d_out = torch.empty(max_rows, 128, device="cuda")
+    d_norms = torch.empty(max_rows, device="cuda")
+    for ids, lens in host_inputs:
+        dev.append((torch.from_numpy(ids).cuda(), torch.from_numpy(lens).cuda()))
+    torch.cuda.synchronize()
+
+    def step(s: int):
+        for j in range(per_step):
+            i = s * per_step + j
+            ids, lens = dev[i]
+            B, L = ids.shape
+            enc.forward_device(ids.data_ptr(), lens.data_ptr(), B, L, d_out.data_ptr(), d_norms.data_ptr(), None,
+                               sp)
+
+    # ---- device-resident timed region
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            step(s)
+    enc.sync(sp)
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local).start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup, args.warmup + args.steps):
+            step(s)
+    e1.record(stream)
+    enc.sync(sp)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms)
+    timed = range(args.warmup * per_step, (args.warmup + args.steps) * per_step)
+    valid_tokens = float(sum(int(host_inputs[i][1].sum()) for i in timed))
+    padded_tokens = float(sum(mine[i].padded_tokens for i in timed))
+    all_valid = sum_over_ranks(valid_tokens)
+    value = all_valid / (ms_max / 1e3)
+    launches = len(timed) * (2 + LAUNCHES_PER_FORWARD_PER_LAYER * n_layers)
+
+    # ---- end to end through the public C ABI (pinned host buffers)
+    pinned = []
+    for ids, lens in host_inputs:
+        B, L = ids.shape
+        pi = torch.from_numpy(ids).pin_memory()
+        pl = torch.from_numpy(lens).pin_memory()
+        po = torch.empty(B, L, 128).pin_memory()
+        pn = torch.empty(B, L).pin_memory()
+        pinned.append((pi, pl, po, pn))
+    l = lib()
+
+    def e2e_batch(i):
+        pi, pl, po, pn = pinned[i]
+        B, L = pi.shape
+        check(l.wc_t5_forward(enc.handle, ctypes.c_void_p(pi.data_ptr()), ctypes.c_void_p(pl.data_ptr()), B, L,
+                              ctypes.c_void_p(po.data_ptr()), ctypes.c_void_p(pn.data_ptr()), None), enc.handle)
+
+    for i in range(args.warmup * per_step):
+        e2e_batch(i)
+    barrier()
+    t0 = time.perf_counter()
+    for i in timed:
+        e2e_batch(i)
+    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    h2d = sum(pinned[i][0].numel() * 4 + pinned[i][1].numel() * 4 for i in timed) / args.steps
+    d2h = sum(pinned[i][2].numel() * 4 + pinned[i][3].numel() * 4 for i in timed) / args.steps
+    e2e_value = all_valid / t_e2e
+
+    result = None
+    if rank == 0:
+        peak, peak_sus, hbm, peak_src = _peaks()
+        roof = None
+        extras = {}
+        if not args.no_extras:
+            roof, extras = kernel_measurements(enc, args, peak, peak_src)
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "config 4 bulk embedding: 131,072 docs, lengths lognormal(5.0,0.7) clip [16,512], "
+                                   f"length-bucketed batches <= {MAX_BATCH_TOKENS} padded tokens, "
+                                   f"{per_step} batches per rank per step",
+                       "model": "XTR-base (12 x 768, d_ff 2048, 12 heads) random-init N(0,0.02) -> Q4_K",
+                       "padded_tokens_per_rank_step": padded_tokens / args.steps,
+                       "valid_tokens_per_rank_step": valid_tokens / args.steps,
+                       "parallelism": f"replicas x{world} (no data-path collective)",
+                       "l2": "per-batch working set (activations of up to 16,384 tokens, ~250 MB) exceeds the 126 MB L2"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "api": "wc_t5_forward (host buffers, blocking per batch)"},
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        if roof:
+            result["roofline"] = roof
+        result.update(extras)
+        if world == 1 and not args.no_cpu:
+            result["cpu_baseline"] = cpu_reference_leg(model, lengths, target_s=args.ref_seconds)
+        print(json.dumps(result), flush=True)
+    enc.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def _time_launches(fn, stream, reps: int, warm: int = 3) -> float:
+    import torch
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps / 1e3  # seconds per launch
+
+
+def kernel_measurements(enc, args, peak, peak_src):
+    """Per-kernel timings for the roofline: the gated-GELU Q4_K GEMM (the
+    dominant kernel, 44% of encoder FLOPs) at one full batch (M = 16,384),
+    plus the other GEMM shapes (config 2, M = 8192) and attention (config 3),
+    each timed with CUDA events on its launch stream."""
+    import torch
+    from witchcraft_b200._lib import check, lib
+    from witchcraft_b200.synth import quantize_q4k
+    l = lib()
+    st = torch.cuda.Stream()
+    sp = ctypes.c_void_p(st.cuda_stream)
+    rng = np.random.default_rng(2)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def wq(n, k):
+        return torch.from_numpy(quantize_q4k(rng.standard_normal((n, k)).astype(np.float32) * 0.02).reshape(-1)).cuda()
+
+    out = {}
+    w0, w1 = wq(2048, 768), wq(2048, 768)
+    wqkv, wo = wq(2304, 768), wq(768, 2048)
+
+    def gemm_case(M, K, N, epi, w, wu):
+        x = torch.randn(M, K, device="cuda").half()
+        y = torch.empty(M, N, device="cuda", dtype=torch.float16 if epi in (0, 1) else torch.float32)
+        f = lambda: check(l.wc_gemm_q4k(P(x), M, K, P(w), P(wu) if wu is not None else None, N, epi, P(y), sp))  # noqa
+        t = _time_launches(f, st, reps=20)
+        flops = 2.0 * M * K * N * (2 if epi == 1 else 1)
+        return t, flops
+
+    t, fl = gemm_case(16384, 768, 2048, 1, w0, w1)
+    achieved = fl / t / 1e12
+    roof = {"bound": "tensor", "kernel": "gemm_q4k_kernel<256,kEpiGeGLU> (wi_0|wi_1 + gated GELU), M=16384 K=768 N=2x2048",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_source": f"{peak_src} dense bf16/f16 burst", "traffic": NCU_TRAFFIC_BYTES,
+            "avg_launch_us": t * 1e6, "algorithmic_flop_per_launch": fl}
+    micro = {}
+    for name, (M, K, N, epi, w, wu) in {"qkv_M8192": (8192, 768, 2304, 0, wqkv, None),
+                                        "wi_geglu_M8192": (8192, 768, 2048, 1, w0, w1),
+                                        "wo_M8192": (8192, 2048, 768, 3, wo, None)}.items():
+        t, fl = gemm_case(M, K, N, epi, w, wu)
+        micro[name] = {"us": t * 1e6, "tflops": fl / t / 1e12, "frac_of_peak": fl / t / 1e12 / peak}
+    # attention, config 3
+    B, L, H = 64, 512, 12
+    lens = np.random.default_rng(4).integers(32, 513, B).astype(np.int32)
+    qkv = torch.randn(B * L, 3 * H * 64, device="cuda").half()
+    ao = torch.empty(B * L, H * 64, device="cuda").half()
+    dl = torch.from_numpy(lens).cuda()
+    bt = torch.randn(32, H, device="cuda") * 0.1
+    f = lambda: check(l.wc_attention(P(qkv), B, L, H, P(dl), P(bt), 32, 128, P(ao), sp))  # noqa: E731
+    t = _time_launches(f, st, reps=20)
+    afl = float(sum(12 * 4 * 64 * int(n) ** 2 for n in lens))
+    micro["attention_config3"] = {"us": t * 1e6, "tflops": afl / t / 1e12, "frac_of_peak": afl / t / 1e12 / peak}
+    return roof, {"microbench": micro, "query_latency": query_latency(enc)}
+
+
+def query_latency(enc, runs: int = 200):
+    """Config 5: 32-token padded queries (lengths U[4, 32]) at batch 1 and 256,
+    device-resident, one forward per timed call (CUDA events)."""
+    import torch
+    res = {}
+    st = torch.cuda.Stream()
+    for B in (1, 256):
+        rng = np.random.default_rng(6)
+        ids = torch.from_numpy(rng.integers(3, 32128, (B, 32)).astype(np.uint32)).cuda()
+        lens = torch.from_numpy(rng.integers(4, 33, B).astype(np.int32)).cuda()
+        out = torch.empty(B * 32, 128, device="cuda")
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
+        for _ in range(10):
+            enc.forward_device(ids.data_ptr(), lens.data_ptr(), B, 32, out.data_ptr(), None, None, st.cuda_stream)
+        for a, b in ev:
+            a.record(st)
+            enc.forward_device(ids.data_ptr(), lens.data_ptr(), B, 32, out.data_ptr(), None, None, st.cuda_stream)
+            b.record(st)
+        enc.sync(st.cuda_stream)
+        torch.cuda.synchronize()
+        t = np.array([a.elapsed_time(b) for a, b in ev])
+        res[f"b{B}"] = {"p50_ms": float(np.percentile(t, 50)), "p99_ms": float(np.percentile(t, 99))}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batches-per-step", type=int, default=8)
+    ap.add_argument("--ref-seconds", type=float, default=8.0)
+    ap.add_argument("--no-extras", action="store_true", help="skip per-kernel timings and query latency")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -19,6 +19,10 @@
  *     mutex); different handles may be used from different threads at once.
  *   - Kernels never trap: a failed in-kernel wait sets a device status word
  *     that the forward call turns into WC_E_TIMEOUT.
+ *   - Numerics: the residual stream, RMSNorm statistics, every accumulation
+ *     and all outputs are f32; tensor-core operands (normalised activations,
+ *     dequantised weights, Q/K/V, softmax weights, gated-GELU output) are f16
+ *     (11-bit significand), saturated to the finite f16 range.
  *   - Functions taking `void* stream` accept a cudaStream_t (NULL = legacy
  *     default stream) and device pointers; they return once the work is
  *     enqueued.
@@ -96,10 +100,10 @@ int wc_t5_dims(const wc_t5* h, int* d_model, int* n_layers, int* d_proj, int* vo
  * k_quants BlockQ4K as used at src/quantized_t5.rs:44). */
 int wc_q4k_dequant(const void* d_blocks, int64_t nblocks, float* d_out, void* stream);
 
-/* Y = X . W^T with X bf16 [M][K] and W Q4_K [N][K/256 blocks]
+/* Y = X . W^T with X f16 [M][K] and W Q4_K [N][K/256 blocks]
  * (QMatMul::forward, src/quantized_t5.rs:39-49; QTiledOp, src/fused_matmul.rs:46-59).
- * epilogue: 0 = bf16 out [M][N]; 1 = gated GELU: gelu_tanh(X.W^T) * (X.W_up^T)
- *           as bf16 [M][N] (T5DenseGatedActDense, src/quantized_t5.rs:231-252;
+ * epilogue: 0 = f16 out [M][N]; 1 = gated GELU: gelu_tanh(X.W^T) * (X.W_up^T)
+ *           as f16 [M][N] (T5DenseGatedActDense, src/quantized_t5.rs:231-252;
  *           QGatedMatMul, src/fused_matmul.rs:138-177), d_w_up required;
  *           2 = f32 residual: out[M][N] += X.W^T (src/fast_ops.rs:42-48);
  *           3 = f32 out [M][N].
@@ -108,7 +112,7 @@ int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const void* d_w_
                 void* d_out, void* stream);
 
 /* Encoder self-attention (src/quantized_t5.rs:426-500) over a padded batch.
- * d_qkv bf16 [B*L][3*H*64] (q | k | v), d_out bf16 [B*L][H*64], d_lengths
+ * d_qkv f16 [B*L][3*H*64] (q | k | v), d_out f16 [B*L][H*64], d_lengths
  * i32 [B], d_bias_table f32 [num_buckets][H] (relative_attention_bias).
  * No 1/sqrt(d) scaling; keys >= lengths[b] are masked. */
 int wc_attention(const void* d_qkv, int B, int L, int H, const int32_t* d_lengths, const float* d_bias_table,

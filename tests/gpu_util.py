@@ -29,15 +29,15 @@ def dequant_gpu(blocks: np.ndarray) -> torch.Tensor:
     return out
 
 
-def gemm_gpu(x_bf16: torch.Tensor, w_blocks: np.ndarray, epilogue: int, w_up_blocks=None, out=None):
-    M, K = x_bf16.shape
+def gemm_gpu(x16: torch.Tensor, w_blocks: np.ndarray, epilogue: int, w_up_blocks=None, out=None):
+    M, K = x16.shape
     N = w_blocks.shape[0]
     dw = q4k_to_device(w_blocks)
     du = q4k_to_device(w_up_blocks) if w_up_blocks is not None else None
     if out is None:
-        dt = torch.bfloat16 if epilogue in (0, 1) else torch.float32
+        dt = torch.float16 if epilogue in (0, 1) else torch.float32
         out = torch.empty(M, N, dtype=dt, device="cuda")
-    check(lib().wc_gemm_q4k(dptr(x_bf16), M, K, dptr(dw), dptr(du) if du is not None else None, N, epilogue,
+    check(lib().wc_gemm_q4k(dptr(x16), M, K, dptr(dw), dptr(du) if du is not None else None, N, epilogue,
                             dptr(out), stream_ptr()))
     torch.cuda.synchronize()
     return out

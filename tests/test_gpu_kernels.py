@@ -51,54 +51,54 @@ def _weights(N, K, seed):
 @pytest.mark.parametrize("epi", [0, 3])
 def test_gemm_store(M, K, N, epi):
     blocks, wd = _weights(N, K, seed=M + N)
-    x = torch.randn(M, K, generator=torch.Generator().manual_seed(2)).cuda().to(torch.bfloat16)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(2)).cuda().to(torch.float16)
     y = gemm_gpu(x, blocks, epi).float()
-    # same bf16-rounded operands, fp32 accumulation
-    ref = x.float() @ wd.to(torch.bfloat16).float().T
-    tol = 2e-2 if epi == 0 else 2e-3
+    # same f16-rounded operands, fp32 accumulation
+    ref = x.float() @ wd.to(torch.float16).float().T
+    tol = 2e-3
     err = (y - ref).abs().max().item() / ref.abs().max().item()
     assert err < tol, err
     # and against the unrounded f32 weights (the reference's numbers)
     ref32 = x.float() @ wd.T
-    assert ((y - ref32).abs().max() / ref32.abs().max()).item() < 3e-2
+    assert ((y - ref32).abs().max() / ref32.abs().max()).item() < 1e-2
 
 
 @pytest.mark.parametrize("M,K,F", [(8192, 768, 2048), (200, 768, 2048), (64, 256, 512)])
 def test_gemm_geglu(M, K, F):
     b0, w0 = _weights(F, K, 10)
     b1, w1 = _weights(F, K, 11)
-    x = torch.randn(M, K, generator=torch.Generator().manual_seed(3)).cuda().to(torch.bfloat16)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(3)).cuda().to(torch.float16)
     y = gemm_gpu(x, b0, 1, w_up_blocks=b1).float()
     xf = x.float()
-    ref = _gelu(xf @ w0.to(torch.bfloat16).float().T) * (xf @ w1.to(torch.bfloat16).float().T)
+    ref = _gelu(xf @ w0.to(torch.float16).float().T) * (xf @ w1.to(torch.float16).float().T)
     err = ((y - ref).abs().max() / ref.abs().max()).item()
-    assert err < 2e-2, err
+    assert err < 5e-3, err
 
 
 def test_gemm_residual_accumulates():
     M, K, N = 333, 2048, 768
     blocks, wd = _weights(N, K, 12)
-    x = torch.randn(M, K).cuda().to(torch.bfloat16)
+    x = torch.randn(M, K).cuda().to(torch.float16)
     base = torch.randn(M, N, device="cuda")
     out = base.clone()
     gemm_gpu(x, blocks, 2, out=out)
-    ref = base + x.float() @ wd.to(torch.bfloat16).float().T
+    ref = base + x.float() @ wd.to(torch.float16).float().T
     assert ((out - ref).abs().max() / ref.abs().max()).item() < 2e-3
 
 
 def test_gemm_rejects_bad_shapes():
     l = lib()
-    x = torch.zeros(8, 300, dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros(8, 300, dtype=torch.float16, device="cuda")
     assert l.wc_gemm_q4k(dptr(x), 8, 300, dptr(x), None, 128, 0, dptr(x), stream_ptr()) == -1
     assert l.wc_gemm_q4k(dptr(x), 8, 256, dptr(x), None, 100, 0, dptr(x), stream_ptr()) == -1
     assert l.wc_gemm_q4k(dptr(x), 8, 256, dptr(x), None, 128, 1, dptr(x), stream_ptr()) == -1
 
 
-def _attention_gpu(qkv_bf16, B, L, H, lengths, bias_tab):
-    out = torch.empty(B * L, H * 64, dtype=torch.bfloat16, device="cuda")
+def _attention_gpu(qkv16, B, L, H, lengths, bias_tab):
+    out = torch.empty(B * L, H * 64, dtype=torch.float16, device="cuda")
     dl = torch.tensor(lengths, dtype=torch.int32, device="cuda")
     db = torch.from_numpy(np.ascontiguousarray(bias_tab, np.float32)).cuda()
-    check(lib().wc_attention(dptr(qkv_bf16), B, L, H, dptr(dl), dptr(db), 32, 128, dptr(out), stream_ptr()))
+    check(lib().wc_attention(dptr(qkv16), B, L, H, dptr(dl), dptr(db), 32, 128, dptr(out), stream_ptr()))
     torch.cuda.synchronize()
     return out
 
@@ -123,7 +123,7 @@ def _attention_torch(qkv, B, L, H, lengths, bias_tab):
 def test_attention_matches_oracle(B, L, lengths):
     H = 12
     g = torch.Generator().manual_seed(B * 1000 + L)
-    qkv = torch.randn(B * L, 3 * H * 64, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(B * L, 3 * H * 64, generator=g).to(torch.float16)
     bias_tab = (np.random.default_rng(L).standard_normal((32, H)) * 0.1).astype(np.float32)
     out = _attention_gpu(qkv.cuda(), B, L, H, lengths, bias_tab).float().cpu().numpy()
     ref = O.attention(qkv.float().numpy(), B, L, H, lengths, bias_tab)
@@ -138,7 +138,7 @@ def test_attention_config3_against_torch():
     B, L, H = 64, 512, 12
     rng = np.random.default_rng(4)
     lengths = rng.integers(32, 513, B).tolist()
-    qkv = torch.randn(B * L, 3 * H * 64, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+    qkv = torch.randn(B * L, 3 * H * 64, generator=torch.Generator().manual_seed(3)).to(torch.float16).cuda()
     bias_tab = (np.random.default_rng(3).standard_normal((32, H)) * 0.1).astype(np.float32)
     out = _attention_gpu(qkv, B, L, H, lengths, bias_tab).float()
     ref = _attention_torch(qkv, B, L, H, lengths, bias_tab)

@@ -4,14 +4,14 @@
 // scaling, + position bias, softmax_last_dim, P.V, transpose back to tokens).
 //
 // Input: the token-major QKV projection [B*L][3*inner] (q | k | v, each
-// H heads x 64), bf16.  Output: [B*L][inner] bf16, token-major, which is the
+// H heads x 64), f16.  Output: [B*L][inner] f16, token-major, which is the
 // layout the O projection reads.  Query rows past a sequence's valid length
 // that fall in an all-padding 64-row tile are written as zeros; keys past the
 // valid length never contribute.
 //
 // Tiling: one CTA per (64 queries, head, sequence), 4 warps x 16 query rows;
 // 64-key K/V tiles double-buffered in shared memory by cp.async; QK^T and PV
-// on the bf16 tensor cores (m16n8k16, f32 accumulate); softmax in f32 with
+// on the f16 tensor cores (m16n8k16, f32 accumulate); softmax in f32 with
 // exp2 and a running max/sum per row kept by the 4 lanes that share it.
 #include "attention.h"
 #include "common.cuh"
@@ -48,9 +48,9 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, u
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -67,8 +67,8 @@ __device__ __forceinline__ int rel_bucket(const BucketThresholds& bt, int delta)
   return f + (delta > 0 ? bt.half : 0);
 }
 
-__global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                                        __nv_bfloat16* __restrict__ out,
+__global__ void __launch_bounds__(128) attention_kernel(const __half* __restrict__ qkv,
+                                                        __half* __restrict__ out,
                                                         const int32_t* __restrict__ lengths, int L, int H,
                                                         const float* __restrict__ bias_tab, BucketThresholds bt) {
   __shared__ __align__(1024) uint8_t sQ[kTile * 128];
@@ -94,17 +94,17 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
     return;
   }
 
-  const __nv_bfloat16* qbase = qkv + seq_row0 * ld + h * kDh;
-  const __nv_bfloat16* kbase = qbase + inner;
-  const __nv_bfloat16* vbase = qbase + 2 * inner;
+  const __half* qbase = qkv + seq_row0 * ld + h * kDh;
+  const __half* kbase = qbase + inner;
+  const __half* vbase = qbase + 2 * inner;
 
-  auto load_tile = [&](uint8_t* dst, const __nv_bfloat16* base, int row0) {
+  auto load_tile = [&](uint8_t* dst, const __half* base, int row0) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int idx = tid + i * 128;
       const int r = idx >> 3, c = idx & 7;
       const bool ok = row0 + r < L;
-      const __nv_bfloat16* src = base + static_cast<size_t>(ok ? row0 + r : 0) * ld + c * 8;
+      const __half* src = base + static_cast<size_t>(ok ? row0 + r : 0) * ld + c * 8;
       cp_async16(smem_u32(dst + tile_off(r, c)), src, ok);
     }
   };
@@ -162,8 +162,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
         const int chunk = 2 * kk + ((lane >> 3) & 1);
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(smem_u32(sK[buf] + tile_off(key, chunk)), b0, b1, b2, b3);
-        mma_bf16_16816(s[2 * np], qf[kk], b0, b1);
-        mma_bf16_16816(s[2 * np + 1], qf[kk], b2, b3);
+        mma_f16_16816(s[2 * np], qf[kk], b0, b1);
+        mma_f16_16816(s[2 * np + 1], qf[kk], b2, b3);
       }
     }
 
@@ -202,8 +202,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
         pv[e] = exp2f((s[nt][e] - row_max[e >> 1]) * kLog2e);
         psum[e >> 1] += pv[e];
       }
-      pf[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16x2(pv[0], pv[1]);
-      pf[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+      pf[nt >> 1][(nt & 1) * 2 + 0] = pack_f16x2(pv[0], pv[1]);
+      pf[nt >> 1][(nt & 1) * 2 + 1] = pack_f16x2(pv[2], pv[3]);
     }
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) row_sum[hr] += psum[hr];
@@ -225,15 +225,15 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
         const int chunk = 2 * dp + (lane >> 4);
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4_trans(smem_u32(sV[buf] + tile_off(key, chunk)), b0, b1, b2, b3);
-        mma_bf16_16816(o[2 * dp], a, b0, b1);
-        mma_bf16_16816(o[2 * dp + 1], a, b2, b3);
+        mma_f16_16816(o[2 * dp], a, b0, b1);
+        mma_f16_16816(o[2 * dp + 1], a, b2, b3);
       }
     }
     __syncthreads();  // buffers of this tile are refilled next iteration
   }
   cp_async_wait<0>();
 
-  // finalise: quad-reduce the row sums, normalise, store bf16
+  // finalise: quad-reduce the row sums, normalise, store f16
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
     row_sum[hr] += __shfl_xor_sync(0xFFFFFFFFu, row_sum[hr], 1);
@@ -244,12 +244,12 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
   for (int hr = 0; hr < 2; ++hr) {
     const int qi = q0 + r_lo + hr * 8;
     if (qi < L) {
-      __nv_bfloat16* dst = out + (seq_row0 + qi) * inner + h * kDh;
+      __half* dst = out + (seq_row0 + qi) * inner + h * kDh;
       const float inv = hr ? inv1 : inv0;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const int d = nt * 8 + 2 * (lane & 3);
-        *reinterpret_cast<uint32_t*>(dst + d) = pack_bf16x2(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv);
+        *reinterpret_cast<uint32_t*>(dst + d) = pack_f16x2_sat(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv);
       }
     }
   }
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
 
 }  // namespace
 
-cudaError_t attention_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, const int32_t* lengths, int B, int L,
+cudaError_t attention_launch(const __half* qkv, __half* out, const int32_t* lengths, int B, int L,
                              int H, const float* bias_tab, const BucketThresholds& bt, cudaStream_t st) {
   if (B <= 0 || L <= 0) return cudaSuccess;
   dim3 grid((L + kTile - 1) / kTile, H, B);

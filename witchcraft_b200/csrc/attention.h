@@ -1,6 +1,6 @@
 // Host-visible declarations of the encoder attention kernel.
 #pragma once
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -16,9 +16,9 @@ struct BucketThresholds {
   int thr[32];   // thr[v] = smallest distance d with bucket_half(d) >= v
 };
 
-// qkv: [B*L][3*H*64] bf16 (q | k | v); out: [B*L][H*64] bf16;
+// qkv: [B*L][3*H*64] f16 (q | k | v); out: [B*L][H*64] f16;
 // lengths: device [B]; bias_tab: device f32 [num_buckets][H].
-cudaError_t attention_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, const int32_t* lengths, int B, int L,
+cudaError_t attention_launch(const __half* qkv, __half* out, const int32_t* lengths, int B, int L,
                              int H, const float* bias_tab, const BucketThresholds& bt, cudaStream_t st);
 
 }  // namespace wc

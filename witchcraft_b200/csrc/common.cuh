@@ -107,8 +107,8 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, f32 accumulate, one CTA.
-__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+// D[tmem] (+)= A[smem] * B[smem]^T, 16-bit inputs, f32 accumulate, one CTA.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -142,7 +142,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
 }
 
 // Shared-memory matrix descriptor (tcgen05 "UMMA" descriptor) for a K-major
-// operand tile stored with the 128-byte swizzle: rows of 64 bf16 (128 B),
+// operand tile stored with the 128-byte swizzle: rows of 64 f16 (128 B),
 // 8-row groups 1024 B apart.  Fields: start address >> 4 in [0,14), leading
 // byte offset >> 4 in [16,30) (unused for swizzled K-major), stride byte
 // offset >> 4 in [32,46), descriptor version 1 in [46,48), layout type in
@@ -157,11 +157,12 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B, f32 D, both K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+// Instruction descriptor for kind::f16 with f16 A/B, f32 D, both K-major
+// (A/B format field 0 = f16, 1 = bf16; both operands must share the type).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
   return (1u << 4)                                // D format f32
-         | (1u << 7)                              // A format bf16
-         | (1u << 10)                             // B format bf16
+         | (0u << 7)                              // A format f16
+         | (0u << 10)                             // B format f16
          | (static_cast<uint32_t>(n >> 3) << 17)  // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24); // M / 16
 }
@@ -172,9 +173,15 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+// Two f32 -> packed f16x2, round to nearest even.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+// Same, saturating to the finite f16 range (+-65504) so an activation that
+// leaves the range stays finite instead of becoming inf.
+__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
+  return pack_f16x2(fminf(fmaxf(lo, -65504.f), 65504.f), fminf(fmaxf(hi, -65504.f), 65504.f));
 }
 
 }  // namespace wc

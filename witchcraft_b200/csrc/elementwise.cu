@@ -38,7 +38,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const uint32_t* __restrict__ ids,
                                      const int32_t* __restrict__ lengths, int L, int M, int D,
                                      const float* __restrict__ w, float eps, float* __restrict__ x,
-                                     __nv_bfloat16* __restrict__ xn) {
+                                     __half* __restrict__ xn) {
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -70,10 +70,10 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
       const float4 w0 = reinterpret_cast<const float4*>(w + e)[0];
       const float4 w1 = reinterpret_cast<const float4*>(w + e)[1];
       uint4 o;
-      o.x = pack_bf16x2(v[c][0] / den * w0.x, v[c][1] / den * w0.y);
-      o.y = pack_bf16x2(v[c][2] / den * w0.z, v[c][3] / den * w0.w);
-      o.z = pack_bf16x2(v[c][4] / den * w1.x, v[c][5] / den * w1.y);
-      o.w = pack_bf16x2(v[c][6] / den * w1.z, v[c][7] / den * w1.w);
+      o.x = pack_f16x2_sat(v[c][0] / den * w0.x, v[c][1] / den * w0.y);
+      o.y = pack_f16x2_sat(v[c][2] / den * w0.z, v[c][3] / den * w0.w);
+      o.z = pack_f16x2_sat(v[c][4] / den * w1.x, v[c][5] / den * w1.y);
+      o.w = pack_f16x2_sat(v[c][6] / den * w1.z, v[c][7] / den * w1.w);
       *reinterpret_cast<uint4*>(xn + static_cast<size_t>(m) * D + e) = o;
     }
   }
@@ -81,7 +81,7 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
 
 // lane owns float4 groups lane + 32*i, i < D/128
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                               __nv_bfloat16* __restrict__ y, int M, int D, float eps) {
+                               __half* __restrict__ y, int M, int D, float eps) {
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -105,8 +105,8 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     if (g < ng) {
       const float4 ww = wr[lane + 32 * g];
       uint2 o;
-      o.x = pack_bf16x2(v[g].x / den * ww.x, v[g].y / den * ww.y);
-      o.y = pack_bf16x2(v[g].z / den * ww.z, v[g].w / den * ww.w);
+      o.x = pack_f16x2_sat(v[g].x / den * ww.x, v[g].y / den * ww.y);
+      o.y = pack_f16x2_sat(v[g].z / den * ww.z, v[g].w / den * ww.w);
       yr[lane + 32 * g] = o;
     }
   }
@@ -123,14 +123,14 @@ cudaError_t q4k_dequant_launch(const uint8_t* blocks, int64_t nblocks, float* ou
 }
 
 cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, const int32_t* lengths, int L, int M,
-                                 int D, const float* w, float eps, float* x, __nv_bfloat16* xn, cudaStream_t st) {
+                                 int D, const float* w, float eps, float* x, __half* xn, cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 256 != 0 || D > kMaxD) return cudaErrorInvalidValue;
   embed_rmsnorm_kernel<<<(M + 7) / 8, 256, 0, st>>>(table, ids, lengths, L, M, D, w, eps, x, xn);
   return cudaGetLastError();
 }
 
-cudaError_t rmsnorm_launch(const float* x, const float* w, __nv_bfloat16* y, int M, int D, float eps,
+cudaError_t rmsnorm_launch(const float* x, const float* w, __half* y, int M, int D, float eps,
                            cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 128 != 0 || D > kMaxD) return cudaErrorInvalidValue;

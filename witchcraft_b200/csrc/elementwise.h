@@ -1,7 +1,7 @@
 // Host-visible declarations of the memory-bound kernels: Q4_K dequant,
 // embedding gather (+ the first RMSNorm) and RMSNorm.
 #pragma once
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -11,12 +11,12 @@ namespace wc {
 cudaError_t q4k_dequant_launch(const uint8_t* blocks, int64_t nblocks, float* out, cudaStream_t st);
 
 // x[m] = dequant(table row ids[m]) (id 0 for positions past a sequence's
-// valid length), xn[m] = bf16(RMSNorm(x[m]) * w).  table: Q4_K [vocab][D/256].
+// valid length), xn[m] = f16(RMSNorm(x[m]) * w).  table: Q4_K [vocab][D/256].
 cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, const int32_t* lengths, int L, int M,
-                                 int D, const float* w, float eps, float* x, __nv_bfloat16* xn, cudaStream_t st);
+                                 int D, const float* w, float eps, float* x, __half* xn, cudaStream_t st);
 
-// y[m] = bf16(x[m] / sqrt(mean(x[m]^2) + eps) * w), D % 128 == 0.
-cudaError_t rmsnorm_launch(const float* x, const float* w, __nv_bfloat16* y, int M, int D, float eps,
+// y[m] = f16(x[m] / sqrt(mean(x[m]^2) + eps) * w), D % 128 == 0.
+cudaError_t rmsnorm_launch(const float* x, const float* w, __half* y, int M, int D, float eps,
                            cudaStream_t st);
 
 }  // namespace wc

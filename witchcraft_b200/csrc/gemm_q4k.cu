@@ -1,23 +1,23 @@
-// Q4_K x bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Q4_K x f16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-//   Y[M, N] = X[M, K] . W[N, K]^T      X: bf16 row-major, W: Q4_K rows
+//   Y[M, N] = X[M, K] . W[N, K]^T      X: f16 row-major, W: Q4_K rows
 //
 // replaces the reference's QMatMul::forward (candle, dequantised to f32 at
 // load on CPU, src/quantized_t5.rs:39-49) and the hybrid path's
 // QTiledOp / QGatedMatMul (src/fused_matmul.rs:46-59,138-177).
 //
 // One CTA computes a 128 x BN output tile.  Warp roles (320 threads):
-//   warp 0      TMA producer: X tiles (128 x 64 bf16, 128-B swizzle) and raw
+//   warp 0      TMA producer: X tiles (128 x 64 f16, 128-B swizzle) and raw
 //               Q4_K super-block tiles (BN rows x 144 B) into smem rings
 //   warp 1      TMEM allocation + the single MMA-issuing thread
-//   warps 2-9   dequant: raw Q4_K (smem) -> bf16 B tiles (BN x 64, 128-B
+//   warps 2-9   dequant: raw Q4_K (smem) -> f16 B tiles (BN x 64, 128-B
 //               swizzled, K-major) in a third ring; then the epilogue
 //               (tcgen05.ld TMEM -> registers -> global)
 // The f32 accumulator (128 lanes x BN columns) lives in TMEM.
 //
 // Epilogues:
-//   kEpiBF16   store bf16                                (Q/K/V projection)
-//   kEpiGeGLU  gelu_tanh(gate) * up -> bf16, the tile's first BN/2 columns
+//   kEpiF16    store f16                                 (Q/K/V projection)
+//   kEpiGeGLU  gelu_tanh(gate) * up -> f16, the tile's first BN/2 columns
 //              are wi_0 rows and the last BN/2 are wi_1 rows of the same
 //              output features (src/quantized_t5.rs:231-252)
 //   kEpiResid  x[m, n] += acc in f32 (O and wo with the residual add of
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
+      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
       bool ok = true;
       for (int t = 0; t < ksteps && ok; ++t) {
         const int sa = t % C::SA;
@@ -149,8 +149,8 @@ __global__ void __launch_bounds__(320, 1)
         const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + sb * C::B_BYTES));
 #pragma unroll
         for (int k = 0; k < C::BK / 16; ++k) {
-          // advance 16 bf16 (32 B) along K inside the swizzle atom
-          tc_mma_bf16(tmem_acc, adesc + 2 * k, bdesc + 2 * k, idesc, (t > 0 || k > 0) ? 1u : 0u);
+          // advance 16 f16 (32 B) along K inside the swizzle atom
+          tc_mma_f16(tmem_acc, adesc + 2 * k, bdesc + 2 * k, idesc, (t > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(&empty_a[sa]);
         tc_commit(&empty_b[sb]);
@@ -198,10 +198,10 @@ __global__ void __launch_bounds__(320, 1)
             float v[8];
             q4k_dequant8(x0, x1, d1, m1, v);
             uint4 o;
-            o.x = pack_bf16x2(v[0], v[1]);
-            o.y = pack_bf16x2(v[2], v[3]);
-            o.z = pack_bf16x2(v[4], v[5]);
-            o.w = pack_bf16x2(v[6], v[7]);
+            o.x = pack_f16x2(v[0], v[1]);
+            o.y = pack_f16x2(v[2], v[3]);
+            o.z = pack_f16x2(v[4], v[5]);
+            o.w = pack_f16x2(v[6], v[7]);
             *reinterpret_cast<uint4*>(bt + sw128_offset(r, hs * 4 + cc)) = o;
           }
         }
@@ -222,22 +222,22 @@ __global__ void __launch_bounds__(320, 1)
     tc_fence_after();
     if (acc_ok) {
       const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
-      if (EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiResid) {
+      if (EPI == kEpiF16 || EPI == kEpiF32 || EPI == kEpiResid) {
         const int n_base = n_tile * BN;
 #pragma unroll 1
         for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
           float v[32];
           tmem_ld_32x32b_x32(tbase + c, v);
           if (m < p.M) {
-            if (EPI == kEpiBF16) {
-              __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + n_base + c;
+            if (EPI == kEpiF16) {
+              __half* out = reinterpret_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + n_base + c;
 #pragma unroll
               for (int i = 0; i < 32; i += 8) {
                 uint4 o;
-                o.x = pack_bf16x2(v[i], v[i + 1]);
-                o.y = pack_bf16x2(v[i + 2], v[i + 3]);
-                o.z = pack_bf16x2(v[i + 4], v[i + 5]);
-                o.w = pack_bf16x2(v[i + 6], v[i + 7]);
+                o.x = pack_f16x2_sat(v[i], v[i + 1]);
+                o.y = pack_f16x2_sat(v[i + 2], v[i + 3]);
+                o.z = pack_f16x2_sat(v[i + 4], v[i + 5]);
+                o.w = pack_f16x2_sat(v[i + 6], v[i + 7]);
                 *reinterpret_cast<uint4*>(out + i) = o;
               }
             } else if (EPI == kEpiF32) {
@@ -267,14 +267,14 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld_32x32b_x32(tbase + c, g);
           tmem_ld_32x32b_x32(tbase + BN / 2 + c, u);
           if (m < p.M) {
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + out_base + c;
+            __half* out = reinterpret_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + out_base + c;
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
               uint4 o;
-              o.x = pack_bf16x2(gelu_tanh(g[i]) * u[i], gelu_tanh(g[i + 1]) * u[i + 1]);
-              o.y = pack_bf16x2(gelu_tanh(g[i + 2]) * u[i + 2], gelu_tanh(g[i + 3]) * u[i + 3]);
-              o.z = pack_bf16x2(gelu_tanh(g[i + 4]) * u[i + 4], gelu_tanh(g[i + 5]) * u[i + 5]);
-              o.w = pack_bf16x2(gelu_tanh(g[i + 6]) * u[i + 6], gelu_tanh(g[i + 7]) * u[i + 7]);
+              o.x = pack_f16x2_sat(gelu_tanh(g[i]) * u[i], gelu_tanh(g[i + 1]) * u[i + 1]);
+              o.y = pack_f16x2_sat(gelu_tanh(g[i + 2]) * u[i + 2], gelu_tanh(g[i + 3]) * u[i + 3]);
+              o.z = pack_f16x2_sat(gelu_tanh(g[i + 4]) * u[i + 4], gelu_tanh(g[i + 5]) * u[i + 5]);
+              o.w = pack_f16x2_sat(gelu_tanh(g[i + 6]) * u[i + 6], gelu_tanh(g[i + 7]) * u[i + 7]);
               *reinterpret_cast<uint4*>(out + i) = o;
             }
           }
@@ -358,7 +358,7 @@ cudaError_t gemm_q4k_launch(int epi, int bn, const CUtensorMap& a, const CUtenso
                             const GemmParams& p, cudaStream_t st) {
   if (bn == 256) {
     switch (epi) {
-      case kEpiBF16: return launch_one<256, kEpiBF16>(a, w0, w1, p, st);
+      case kEpiF16: return launch_one<256, kEpiF16>(a, w0, w1, p, st);
       case kEpiGeGLU: return launch_one<256, kEpiGeGLU>(a, w0, w1, p, st);
       case kEpiResid: return launch_one<256, kEpiResid>(a, w0, w1, p, st);
       case kEpiF32: return launch_one<256, kEpiF32>(a, w0, w1, p, st);
@@ -366,7 +366,7 @@ cudaError_t gemm_q4k_launch(int epi, int bn, const CUtensorMap& a, const CUtenso
     }
   } else if (bn == 128) {
     switch (epi) {
-      case kEpiBF16: return launch_one<128, kEpiBF16>(a, w0, w1, p, st);
+      case kEpiF16: return launch_one<128, kEpiF16>(a, w0, w1, p, st);
       case kEpiGeGLU: return launch_one<128, kEpiGeGLU>(a, w0, w1, p, st);
       case kEpiResid: return launch_one<128, kEpiResid>(a, w0, w1, p, st);
       case kEpiF32: return launch_one<128, kEpiF32>(a, w0, w1, p, st);

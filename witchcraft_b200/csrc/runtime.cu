@@ -4,17 +4,17 @@
 // Forward (one padded batch of B sequences x L tokens, M = B*L rows):
 //   embed_rmsnorm      x = dequant(embedding rows), xn = RMSNorm_0(x)
 //   per layer l:
-//     gemm  kEpiBF16   qkv = xn . [Wq|Wk|Wv]^T                (bf16 [M][3*inner])
-//     attention        att = softmax(QK^T + bias, key mask) V (bf16 [M][inner])
+//     gemm  kEpiF16   qkv = xn . [Wq|Wk|Wv]^T                (f16 [M][3*inner])
+//     attention        att = softmax(QK^T + bias, key mask) V (f16 [M][inner])
 //     gemm  kEpiResid  x += att . Wo^T                        (f32)
 //     rmsnorm          xn = RMSNorm_ff(x)
-//     gemm  kEpiGeGLU  h = gelu(xn . Wi0^T) * (xn . Wi1^T)    (bf16 [M][d_ff])
+//     gemm  kEpiGeGLU  h = gelu(xn . Wi0^T) * (xn . Wi1^T)    (f16 [M][d_ff])
 //     gemm  kEpiResid  x += h . Wwo^T
 //     rmsnorm          xn = RMSNorm_{next attn | final}(x)
 //   gemm  kEpiProj     out = xn . Wlin^T, norms, out / norm   (f32 [M][128])
 // following T5Stack::forward / T5Block::forward / T5EncoderModel::forward
 // (src/quantized_t5.rs:654-670, 598-628, 698-701).  The residual stream x
-// stays f32; GEMM operands are bf16 with f32 accumulation in TMEM.
+// stays f32; GEMM and attention operands are f16 with f32 accumulation.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <string.h>
@@ -59,7 +59,7 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// bf16 activation matrix [rows][K], box 64 x 128, 128-byte swizzle.
+// f16 activation matrix [rows][K], box 64 x 128, 128-byte swizzle.
 bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
@@ -67,7 +67,7 @@ bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K) {
   cuuint64_t strides[1] = {K * 2};
   cuuint32_t box[2] = {64, 128};
   cuuint32_t es[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -115,7 +115,7 @@ struct wc_t5 {
   int cap_b = 0;
   uint8_t* ws = nullptr;
   float* x = nullptr;
-  __nv_bfloat16 *xn = nullptr, *qkv = nullptr, *att = nullptr, *hbuf = nullptr;
+  __half *xn = nullptr, *qkv = nullptr, *att = nullptr, *hbuf = nullptr;
   CUtensorMap tm_xn, tm_att, tm_h;
   // host-API staging
   uint32_t* d_ids = nullptr;
@@ -172,10 +172,10 @@ int ensure_workspace(wc_t5* h, int64_t rows, int B) {
     return cuda_fail(h, e, "workspace allocation");
   }
   h->x = reinterpret_cast<float*>(h->ws + o_x);
-  h->xn = reinterpret_cast<__nv_bfloat16*>(h->ws + o_xn);
-  h->qkv = reinterpret_cast<__nv_bfloat16*>(h->ws + o_qkv);
-  h->att = reinterpret_cast<__nv_bfloat16*>(h->ws + o_att);
-  h->hbuf = reinterpret_cast<__nv_bfloat16*>(h->ws + o_h);
+  h->xn = reinterpret_cast<__half*>(h->ws + o_xn);
+  h->qkv = reinterpret_cast<__half*>(h->ws + o_qkv);
+  h->att = reinterpret_cast<__half*>(h->ws + o_att);
+  h->hbuf = reinterpret_cast<__half*>(h->ws + o_h);
   h->d_ids = reinterpret_cast<uint32_t*>(h->ws + o_ids);
   h->d_len = reinterpret_cast<int32_t*>(h->ws + o_len);
   h->d_out = reinterpret_cast<float*>(h->ws + o_out);
@@ -219,7 +219,7 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = gemm(h, kEpiBF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, M, 3 * I, D, h->qkv, 3 * I, st)))
+    if ((rc = gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, M, 3 * I, D, h->qkv, 3 * I, st)))
       return rc;
     if ((e = attention_launch(h->qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
@@ -348,6 +348,17 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
       return rc;
   }
 
+  // Dequantised weights are tensor-core operands in f16: refuse checkpoints
+  // whose Q4_K scales could produce values outside the f16 range.
+  {
+    std::vector<const GgufTensor*> gemm_w = {g_proj};
+    for (auto& x : lt) gemm_w.insert(gemm_w.end(), {x.q, x.k, x.v, x.o, x.wi0, x.wi1, x.wo});
+    for (const GgufTensor* g : gemm_w) {
+      const double b = q4k_max_abs_bound(g->data, g->nbytes / 144);
+      if (!(b <= 65504.0))
+        return fail(nullptr, WC_E_UNSUPPORTED, "tensor " + g->name + " has Q4_K scales outside the f16 operand range");
+    }
+  }
   int ndev = wc_t5_device_count();
   if (device_ordinal < 0 || device_ordinal >= ndev)
     return fail(nullptr, WC_E_CUDA,
@@ -443,7 +454,7 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
   h->final_ln = reinterpret_cast<float*>(h->arena + o_fln);
   h->rel_bias = reinterpret_cast<float*>(h->arena + o_bias);
   h->bt = t5_bucket_thresholds(cfg.num_buckets, cfg.max_distance, kMaxL);
-  h->bn_qkv = gemm_q4k_bn_for(kEpiBF16, 3 * I);
+  h->bn_qkv = gemm_q4k_bn_for(kEpiF16, 3 * I);
   h->bn_o = gemm_q4k_bn_for(kEpiResid, D);
   h->bn_wi = gemm_q4k_bn_for(kEpiGeGLU, 2 * F);
   h->bn_wo = gemm_q4k_bn_for(kEpiResid, D);
@@ -462,7 +473,7 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
     w.wo = h->arena + lo[l].wo;
     w.ln0 = reinterpret_cast<float*>(h->arena + lo[l].ln0);
     w.ln1 = reinterpret_cast<float*>(h->arena + lo[l].ln1);
-    ok = make_q4k_map(&w.tm_qkv, w.qkv, 3 * I, D, gemm_q4k_w_box_rows(kEpiBF16, h->bn_qkv)) &&
+    ok = make_q4k_map(&w.tm_qkv, w.qkv, 3 * I, D, gemm_q4k_w_box_rows(kEpiF16, h->bn_qkv)) &&
          make_q4k_map(&w.tm_o, w.o, D, I, gemm_q4k_w_box_rows(kEpiResid, h->bn_o)) &&
          make_q4k_map(&w.tm_wi0, w.wi0, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
          make_q4k_map(&w.tm_wi1, w.wi1, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
@@ -605,7 +616,7 @@ extern "C" int wc_attention(const void* d_qkv, int B, int L, int H, const int32_
       num_buckets < 2 || num_buckets > 64 || max_distance < 1)
     return WC_E_INVALID_ARG;
   const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
-  return attention_launch(static_cast<const __nv_bfloat16*>(d_qkv), static_cast<__nv_bfloat16*>(d_out), d_lengths,
+  return attention_launch(static_cast<const __half*>(d_qkv), static_cast<__half*>(d_out), d_lengths,
                           B, L, H, d_bias_table, bt, static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? WC_OK
              : WC_E_CUDA;

@@ -168,6 +168,34 @@ bool gguf_parse(const uint8_t* buf, size_t len, std::unordered_map<std::string, 
 
 namespace {
 
+double half_bits_to_double(uint16_t h) {
+  const int e = (h >> 10) & 0x1f, m = h & 0x3ff;
+  double v;
+  if (e == 0)
+    v = ldexp(static_cast<double>(m), -24);
+  else if (e == 31)
+    v = m ? NAN : INFINITY;
+  else
+    v = ldexp(static_cast<double>(m | 0x400), e - 25);
+  return (h & 0x8000) ? -v : v;
+}
+
+}  // namespace
+
+double q4k_max_abs_bound(const uint8_t* blocks, size_t nblocks) {
+  double mx = 0.0;
+  for (size_t b = 0; b < nblocks; ++b) {
+    const uint8_t* p = blocks + b * 144;
+    const double d = fabs(half_bits_to_double(static_cast<uint16_t>(p[0] | (p[1] << 8))));
+    const double dm = fabs(half_bits_to_double(static_cast<uint16_t>(p[2] | (p[3] << 8))));
+    const double v = d * 63.0 * 15.0 + dm * 63.0;
+    if (!(v <= mx)) mx = v;  // also propagates NaN
+  }
+  return mx;
+}
+
+namespace {
+
 const char* find_key(const char* json, const char* key) {
   const std::string pat = std::string("\"") + key + "\"";
   const char* p = strstr(json, pat.c_str());

@@ -37,6 +37,10 @@ struct T5Config {
   bool gated_gelu = false;
 };
 
+// Upper bound of |d*sc*q - dmin*m| over nblocks Q4_K super-blocks (the
+// largest magnitude a dequantised weight can take).
+double q4k_max_abs_bound(const uint8_t* blocks, size_t nblocks);
+
 // Parses the fields of config.json the reference's Config reads
 // (src/quantized_t5.rs:90-115).  Returns false with *err on a missing field.
 bool config_parse(const char* json, T5Config* cfg, std::string* err);
