@@ -416,6 +416,36 @@ def query_latency(enc, runs: int = 200):
     return res
 
 
+def profile_kernel(name: str, m: int, launches: int = 5):
+    """A few launches of one kernel (for an ncu capture of that kernel alone)."""
+    import torch
+    from witchcraft_b200._lib import check, lib
+    from witchcraft_b200.synth import quantize_q4k
+    l = lib()
+    rng = np.random.default_rng(2)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def wq(n, k):
+        return torch.from_numpy(quantize_q4k(rng.standard_normal((n, k)).astype(np.float32) * 0.02).reshape(-1)).cuda()
+    if name == "attention":
+        B, L, H = 64, 512, 12
+        lens = torch.from_numpy(np.random.default_rng(4).integers(32, 513, B).astype(np.int32)).cuda()
+        qkv = torch.randn(B * L, 3 * H * 64, device="cuda").half()
+        out = torch.empty(B * L, H * 64, device="cuda").half()
+        bt = torch.randn(32, H, device="cuda") * 0.1
+        f = lambda: check(l.wc_attention(P(qkv), B, L, H, P(lens), P(bt), 32, 128, P(out), None))  # noqa: E731
+    else:
+        K, N, epi = {"geglu": (768, 2048, 1), "qkv": (768, 2304, 0), "wo": (2048, 768, 2)}[name]
+        w, wu = wq(N, K), (wq(N, K) if epi == 1 else None)
+        x = torch.randn(m, K, device="cuda").half()
+        y = torch.zeros(m, N, device="cuda", dtype=torch.float16 if epi in (0, 1) else torch.float32)
+        f = lambda: check(l.wc_gemm_q4k(P(x), m, K, P(w), P(wu) if wu is not None else None, N, epi, P(y), None))  # noqa: E731
+    for _ in range(launches):
+        f()
+    torch.cuda.synchronize()
+    print(json.dumps({"profiled": name, "m": m, "launches": launches}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -426,7 +456,13 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=8.0)
     ap.add_argument("--no-extras", action="store_true", help="skip per-kernel timings and query latency")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile-kernel", choices=["geglu", "qkv", "wo", "attention"], default=None,
+                    help="only launch one kernel a few times (for ncu)")
+    ap.add_argument("--m", type=int, default=16384, help="GEMM rows for --profile-kernel")
     args = ap.parse_args()
+    if args.profile_kernel:
+        profile_kernel(args.profile_kernel, args.m)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

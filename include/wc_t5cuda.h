@@ -87,6 +87,23 @@ int wc_t5_forward(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, 
 int wc_t5_forward_device(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengths, int B, int L, float* d_out,
                          float* d_norms, float* d_out_normalised, void* stream);
 
+/* Same computation as wc_t5_forward_device, for callers that must not
+ * allocate GPU memory during a call: a real-time query path that cannot
+ * afford cudaMalloc's implicit device synchronisation, or a host that owns
+ * and pre-reserves all device memory itself.  (No counterpart in the
+ * reference, whose CPU path has no device memory.)  The activations live in
+ * one fixed 8 MiB array that every GPU loading this library holds until the
+ * process exits, instead of the handle's workspace; B*L is limited to what
+ * fits (about 560 tokens at XTR-base dimensions) and larger calls return
+ * WC_E_INVALID_ARG with the limit in the message.  The first call on a device
+ * looks up the array's device address (and loads the module there), so make
+ * it before any stream capture.  All calls on a device share the array and
+ * the handle's status word: calls that overlap on the GPU race, so serialise
+ * them (one stream, or wait between calls).  Errors are reported like
+ * wc_t5_forward_device (check with wc_t5_sync). */
+int wc_t5_forward_device_noalloc(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengths, int B, int L,
+                                 float* d_out, float* d_norms, float* d_out_normalised, void* stream);
+
 /* Wait for the handle's work on `stream` and report any in-kernel failure. */
 int wc_t5_sync(wc_t5* h, void* stream);
 

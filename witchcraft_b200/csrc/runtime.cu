@@ -629,3 +629,122 @@ extern "C" int wc_t5_relative_bucket(int query, int key, int num_buckets, int ma
   const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
   return t5_bucket_from_thresholds(bt, key - query);
 }
+
+// ---------------------------------------------------------------- no-allocation forward
+//
+// wc_t5_forward_device_noalloc runs the same kernels as wc_t5_forward_device
+// but keeps its activations (the per-call scratch) in the fixed device array
+// below instead of the handle's workspace, so a call never allocates device
+// memory.  The array exists once per GPU that loads this library and is held
+// until the process exits.
+
+static constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace wc {
+namespace {
+
+struct NoAllocLayout {
+  size_t x, xn, qkv, att, h, total;
+};
+
+NoAllocLayout noalloc_layout(const wc_t5* h, int64_t M) {
+  const size_t D = h->cfg.d_model, F = h->cfg.d_ff, I = h->inner;
+  NoAllocLayout l{};
+  size_t off = 0;
+  l.x = off; off = align256(off + M * D * 4);
+  l.xn = off; off = align256(off + M * D * 2);
+  l.qkv = off; off = align256(off + M * 3 * I * 2);
+  l.att = off; off = align256(off + M * I * 2);
+  l.h = off; off = align256(off + M * F * 2);
+  l.total = off;
+  return l;
+}
+
+// Device address of g_noalloc_scratch on the current device.  Looked up once
+// per device (the host-side name of a __device__ array is not a device
+// address); this first lookup also loads the module on that device.
+uint8_t* noalloc_scratch_ptr(int dev, cudaError_t* err) {
+  static uint8_t* ptrs[64] = {};
+  static std::mutex mu;
+  *err = cudaSuccess;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<uint8_t*>(p);
+  }
+  return ptrs[dev];
+}
+
+// The launch sequence of forward_device over caller-provided activation
+// buffers (x, xn, qkv, att, hbuf) and their tensor maps.
+int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half* hbuf, const CUtensorMap& tm_xn,
+               const CUtensorMap& tm_att, const CUtensorMap& tm_h, const uint32_t* ids, const int32_t* lengths,
+               int B, int L, float* out, float* norms, float* outn, cudaStream_t st) {
+  const T5Config& c = h->cfg;
+  const int D = c.d_model, F = c.d_ff, I = h->inner, H = c.num_heads;
+  const int M = B * L;
+  cudaError_t e;
+  if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, x, xn, st)) !=
+      cudaSuccess)
+    return cuda_fail(h, e, "embedding launch");
+  int rc;
+  for (int l = 0; l < c.num_layers; ++l) {
+    LayerW& w = h->layers[l];
+    if ((rc = gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, M, 3 * I, D, qkv, 3 * I, st))) return rc;
+    if ((e = attention_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
+      return cuda_fail(h, e, "attention launch");
+    if ((rc = gemm(h, kEpiResid, h->bn_o, tm_att, w.tm_o, w.tm_o, M, D, I, x, D, st))) return rc;
+    if ((e = rmsnorm_launch(x, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    if ((rc = gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, M, 2 * F, D, hbuf, F, st))) return rc;
+    if ((rc = gemm(h, kEpiResid, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, M, D, F, x, D, st))) return rc;
+    const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
+    if ((e = rmsnorm_launch(x, next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+  }
+  return gemm(h, kEpiProj, 128, tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
+              lengths, L);
+}
+
+}  // namespace
+}  // namespace wc
+
+extern "C" int wc_t5_forward_device_noalloc(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengths, int B,
+                                            int L, float* d_out, float* d_norms, float* d_outn, void* stream) {
+  if (!h) return WC_E_INVALID_ARG;
+  if (!d_ids || !d_lengths || !d_out || B < 1 || L < 1 || L > kMaxL)
+    return fail(h, WC_E_INVALID_ARG, "invalid ids/lengths/out pointer or B, L out of range (1 <= L <= 2048)");
+  DeviceGuard g(h->device);
+  const int64_t M = static_cast<int64_t>(B) * L;
+  const NoAllocLayout lay = noalloc_layout(h, M);
+  if (lay.total > kNoAllocScratchBytes) {
+    const NoAllocLayout one = noalloc_layout(h, 1);
+    int64_t max_tokens = static_cast<int64_t>(kNoAllocScratchBytes / one.total);
+    while (max_tokens > 0 && noalloc_layout(h, max_tokens).total > kNoAllocScratchBytes) --max_tokens;
+    return fail(h, WC_E_INVALID_ARG,
+                "B*L = " + std::to_string(M) + " tokens needs " + std::to_string(lay.total) +
+                    " bytes of scratch; the no-allocation forward has " + std::to_string(kNoAllocScratchBytes) +
+                    " (at most " + std::to_string(max_tokens) + " tokens per call for this model)");
+  }
+  cudaError_t e;
+  uint8_t* base = noalloc_scratch_ptr(h->device, &e);
+  if (!base) return cuda_fail(h, e, "cudaGetSymbolAddress of the no-allocation scratch");
+  float* x = reinterpret_cast<float*>(base + lay.x);
+  __half* xn = reinterpret_cast<__half*>(base + lay.xn);
+  __half* qkv = reinterpret_cast<__half*>(base + lay.qkv);
+  __half* att = reinterpret_cast<__half*>(base + lay.att);
+  __half* hb = reinterpret_cast<__half*>(base + lay.h);
+  CUtensorMap tm_xn, tm_att, tm_h;
+  if (!make_act_map(&tm_xn, xn, M, h->cfg.d_model) || !make_act_map(&tm_att, att, M, h->inner) ||
+      !make_act_map(&tm_h, hb, M, h->cfg.d_ff))
+    return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a no-allocation scratch buffer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The status word was allocated with the handle; clear it for this call.
+  if ((e = cudaMemsetAsync(h->d_status, 0, 4, st)) != cudaSuccess) return cuda_fail(h, e, "status reset");
+  return forward_on(h, x, xn, qkv, att, hb, tm_xn, tm_att, tm_h, d_ids, d_lengths, B, L, d_out, d_norms, d_outn, st);
+}
