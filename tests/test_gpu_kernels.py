@@ -46,8 +46,10 @@ def _weights(N, K, seed):
     return blocks, wd
 
 
+# M >= 512 with N % 256 == 0 runs the 2-SM persistent kernel, the rest the 1-SM kernel
 @pytest.mark.parametrize("M,K,N", [(8192, 768, 2304), (8192, 2048, 768), (1, 768, 768), (77, 768, 2304),
-                                   (300, 2048, 768), (129, 256, 128), (2048, 768, 128)])
+                                   (300, 2048, 768), (129, 256, 128), (2048, 768, 128), (511, 768, 768),
+                                   (512, 768, 768), (1000, 2048, 768), (16384, 768, 256), (700, 256, 512)])
 @pytest.mark.parametrize("epi", [0, 3])
 def test_gemm_store(M, K, N, epi):
     blocks, wd = _weights(N, K, seed=M + N)
@@ -63,7 +65,8 @@ def test_gemm_store(M, K, N, epi):
     assert ((y - ref32).abs().max() / ref32.abs().max()).item() < 1e-2
 
 
-@pytest.mark.parametrize("M,K,F", [(8192, 768, 2048), (200, 768, 2048), (64, 256, 512)])
+@pytest.mark.parametrize("M,K,F", [(8192, 768, 2048), (200, 768, 2048), (64, 256, 512), (1300, 768, 2048),
+                                   (600, 256, 512)])
 def test_gemm_geglu(M, K, F):
     b0, w0 = _weights(F, K, 10)
     b1, w1 = _weights(F, K, 11)
@@ -75,8 +78,9 @@ def test_gemm_geglu(M, K, F):
     assert err < 5e-3, err
 
 
-def test_gemm_residual_accumulates():
-    M, K, N = 333, 2048, 768
+@pytest.mark.parametrize("M", [333, 4000])
+def test_gemm_residual_accumulates(M):
+    K, N = 2048, 768
     blocks, wd = _weights(N, K, 12)
     x = torch.randn(M, K).cuda().to(torch.float16)
     base = torch.randn(M, N, device="cuda")

@@ -1,0 +1,480 @@
+// Q4_K x f16 GEMM on pairs of SMs (tcgen05 cta_group::2), persistent, with a
+// double-buffered TMEM accumulator so the epilogue of one tile overlaps the
+// main loop of the next.  Same contract as gemm_q4k.cu
+// (Y[M, N] = X[M, K] . W[N, K]^T, W in Q4_K rows) and the same epilogues; used
+// for the large-M encoder GEMMs (QKV, O, wi_0|wi_1 + gated GELU, wo).
+//
+// A cluster of two CTAs (one per SM) owns a 256 x 256 output tile:
+//   - each CTA TMA-loads its own 128 rows of X per 64-wide K step;
+//   - each CTA dequantises its own half of the B tile (128 weight rows) from
+//     raw Q4_K super-blocks into f16, so the per-SM dequant work is half of
+//     what a 1-SM 128 x 256 tile needs for the same tensor-core work;
+//   - the even CTA's single MMA thread issues tcgen05.mma.cta_group::2
+//     (M = 256, N = 256) reading A and B from both CTAs' shared memory;
+//   - each CTA's TMEM holds the f32 accumulator of its 128 rows x 256 columns,
+//     twice (512 columns), and its epilogue warps drain one buffer while the
+//     MMAs fill the other.
+// For the gated GELU the even CTA's B half is wi_0 rows and the odd CTA's is
+// the wi_1 rows of the same 128 features, so accumulator columns [0, 128) are
+// gate and [128, 256) are up for every row.
+//
+// Warp roles (448 threads per CTA):
+//   warp 0      TMA producer (X stages; raw Q4_K stages)
+//   warp 1      TMEM allocation; MMA issue (even CTA, one thread)
+//   warps 2-9   dequant: raw Q4_K -> f16 K-major 128-B-swizzled B stages
+//   warps 10-13 epilogue: tcgen05.ld -> registers -> global
+// Cross-CTA signalling: X loads of both CTAs complete on the even CTA's
+// barrier; dequant and epilogue warps arrive on the even CTA's barriers
+// through shared::cluster addresses; MMA completion is committed to both
+// CTAs' barriers (tcgen05.commit multicast).  No TMA load is multicast.
+#include "common.cuh"
+#include "gemm2_q4k.h"
+#include "q4k.cuh"
+
+#include <algorithm>
+
+namespace wc {
+
+namespace {
+
+constexpr int kBM = 256;          // rows per cluster tile (128 per CTA)
+constexpr int kBN = 256;          // columns per tile (128 weight rows per CTA)
+constexpr int kBK = 64;
+constexpr int kHalfN = kBN / 2;   // weight rows dequantised by one CTA
+constexpr int kSA = 6;            // X ring depth
+constexpr int kSW = 3;            // raw Q4_K ring depth (super-blocks)
+constexpr int kSB = 4;            // dequantised B ring depth
+constexpr int kABytes = 128 * kBK * 2;
+constexpr int kWBytes = kHalfN * 144;
+constexpr int kBBytes = kHalfN * kBK * 2;
+constexpr int kOffA = 0;
+constexpr int kOffW = kOffA + kSA * kABytes;
+constexpr int kOffB = kOffW + kSW * kWBytes;
+constexpr int kOffBar = kOffB + kSB * kBBytes;
+constexpr int kSmem = 1024 + kOffBar + 512;
+constexpr int kThreads = 448;
+constexpr int kDequantWarps = 8;
+constexpr int kEpiWarps = 4;
+constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t num_clusters() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same-offset object in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait (cluster-scope acquire) for barriers other CTAs arrive on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicOr(status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+// 2-D TMA load into this CTA's smem whose completion is counted on the
+// barrier at cluster address `bar_cluster` (the even CTA's barrier).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the same-offset barrier of both CTAs when this thread's
+// previously issued MMAs complete.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Packed f32x2 arithmetic (one instruction for two lanes of f32 on sm_100).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// f16x2 of the two f32 lanes, round to nearest even.
+__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
+  return pack_f16x2(__uint_as_float(static_cast<uint32_t>(v)), __uint_as_float(static_cast<uint32_t>(v >> 32)));
+}
+
+// 8 weights from the nibbles in the bytes of x0, x1 (0..15 each):
+// d1*q - m1 exactly as the reference (see q4k.cuh), then f16.
+__device__ __forceinline__ uint4 dequant8_f16(uint32_t x0, uint32_t x1, uint64_t d1, uint64_t negm1) {
+  const uint64_t kNeg223 = f2(-8388608.0f, -8388608.0f);
+  uint32_t o[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t x = p < 2 ? x0 : x1;
+    const uint32_t b = (p & 1) * 2;
+    const uint64_t magic = (static_cast<uint64_t>(__byte_perm(x, 0x4B000000u, 0x7440u | (b + 1))) << 32) |
+                           __byte_perm(x, 0x4B000000u, 0x7440u | b);
+    const uint64_t q = f2_add(magic, kNeg223);
+    o[p] = f2_to_h2(f2_fma(d1, q, negm1));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ float gelu_tanh2(float g) {
+  return 0.5f * g * (1.0f + tanhf(0.7978845608f * (g + 0.044715f * g * g * g)));
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm2_q4k_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
+                     const __grid_constant__ CUtensorMap tmW1, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem + kOffA;
+  uint8_t* sW = smem + kOffW;
+  uint8_t* sB = smem + kOffB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full_a = bars;                 // [kSA]  even CTA: X bytes of both CTAs
+  uint64_t* empty_a = full_a + kSA;        // [kSA]  each CTA: MMA done with the stage
+  uint64_t* full_w = empty_a + kSA;        // [kSW]  local raw Q4_K landed
+  uint64_t* empty_w = full_w + kSW;        // [kSW]  local dequant warps done with it
+  uint64_t* full_b = empty_w + kSW;        // [kSB]  even CTA: 16 dequant warps of both CTAs
+  uint64_t* empty_b = full_b + kSB;        // [kSB]  each CTA: MMA done with the stage
+  uint64_t* acc_full = empty_b + kSB;      // [2]    each CTA: accumulator ready
+  uint64_t* acc_empty = acc_full + 2;      // [2]    even CTA: 8 epilogue warps drained it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int ksteps = p.K / kBK;
+  const int kblocks = p.K / 256;
+  const int m_tiles = (p.M + kBM - 1) / kBM;
+  const int n_tiles = p.N / kBN;
+  const int n_total = m_tiles * n_tiles;
+  const int cid = static_cast<int>(cluster_id());
+  const int ncl = static_cast<int>(num_clusters());
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSA; ++i) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&empty_a[i], 1);
+    }
+    for (int i = 0; i < kSW; ++i) {
+      mbar_init(&full_w[i], 1);
+      mbar_init(&empty_w[i], kDequantWarps);
+    }
+    for (int i = 0; i < kSB; ++i) {
+      mbar_init(&full_b[i], 2 * kDequantWarps);
+      mbar_init(&empty_b[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * kEpiWarps);
+    }
+    mbar_fence_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW0);
+    tma_prefetch_desc(&tmW1);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const CUtensorMap* wmap = (EPI == kEpiGeGLU && rank == 1) ? &tmW1 : &tmW0;
+      uint32_t ia = 0, iw = 0;
+      bool ok = true;
+      for (int tile = cid; tile < n_total && ok; tile += ncl) {
+        const int m0 = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128;
+        const int nt = tile % n_tiles;
+        const int w_row0 = EPI == kEpiGeGLU ? nt * kHalfN : nt * kBN + static_cast<int>(rank) * kHalfN;
+        for (int t = 0; t < ksteps; ++t) {
+          if ((t & 3) == 0) {
+            const uint32_t sw = iw % kSW;
+            if (!(ok = mbar_wait(&empty_w[sw], ((iw / kSW) & 1) ^ 1, p.status))) break;
+            mbar_arrive_expect_tx(&full_w[sw], kWBytes);
+            tma_load_2d(sW + sw * kWBytes, wmap, &full_w[sw], (t >> 2) * 144, w_row0);
+            ++iw;
+          }
+          const uint32_t sa = ia % kSA;
+          if (!(ok = mbar_wait(&empty_a[sa], ((ia / kSA) & 1) ^ 1, p.status))) break;
+          if (leader) mbar_arrive_expect_tx(&full_a[sa], 2 * kABytes);
+          tma_load_2d_pair(sA + sa * kABytes, &tmA, map_to_rank(&full_a[sa], 0), t * kBK, m0);
+          ++ia;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN);
+      uint32_t ia = 0, ib = 0, it = 0;
+      bool ok = true;
+      for (int tile = cid; tile < n_total && ok; tile += ncl, ++it) {
+        const uint32_t buf = it & 1;
+        if (!(ok = mbar_wait_cluster(&acc_empty[buf], ((it >> 1) & 1) ^ 1, p.status))) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * kBN;
+        for (int t = 0; t < ksteps; ++t, ++ia, ++ib) {
+          const uint32_t sa = ia % kSA, sb = ib % kSB;
+          ok = mbar_wait_cluster(&full_a[sa], (ia / kSA) & 1, p.status) &&
+               mbar_wait_cluster(&full_b[sb], (ib / kSB) & 1, p.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + sa * kABytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + sb * kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            tc_mma_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (t > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(&empty_a[sa]);
+          tc_commit_pair(&empty_b[sb]);
+        }
+        if (ok) tc_commit_pair(&acc_full[buf]);
+      }
+    }
+  } else if (warp < 2 + kDequantWarps) {
+    // ------------------------------------------------------------ dequant
+    const int td = threadIdx.x - 64;   // 0..255
+    const int r = td & (kHalfN - 1);   // weight row within this CTA's half
+    const int hs = td >> 7;            // low (0) / high (1) nibble: sub-block 2ks + hs
+    const uint32_t full_b_leader0 = map_to_rank(&full_b[0], 0);
+    uint32_t iw = 0, ib = 0;
+    bool ok = true;
+    for (int tile = cid; tile < n_total && ok; tile += ncl) {
+      for (int kb = 0; kb < kblocks && ok; ++kb, ++iw) {
+        const uint32_t sw = iw % kSW;
+        if (!(ok = mbar_wait(&full_w[sw], (iw / kSW) & 1, p.status))) break;
+        const uint8_t* blk = sW + sw * kWBytes + r * 144;
+        const Q4KScales sc = q4k_load_scales(blk);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks, ++ib) {
+          const uint32_t sb = ib % kSB;
+          if (!(ok = mbar_wait(&empty_b[sb], ((ib / kSB) & 1) ^ 1, p.status))) break;
+          float d1f, m1f;
+          q4k_sub_scale(sc, 2 * ks + hs, d1f, m1f);
+          const uint64_t d1 = f2(d1f, d1f), negm1 = f2(-m1f, -m1f);
+          const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * ks);
+          const uint4 q0 = qp[0], q1 = qp[1];
+          const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          uint8_t* bt = sB + sb * kBBytes;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const uint32_t x0 = (qw[2 * cc] >> (4 * hs)) & 0x0F0F0F0Fu;
+            const uint32_t x1 = (qw[2 * cc + 1] >> (4 * hs)) & 0x0F0F0F0Fu;
+            *reinterpret_cast<uint4*>(bt + sw128_offset(r, hs * 4 + cc)) = dequant8_f16(x0, x1, d1, negm1);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(full_b_leader0 + sb * 8);
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&empty_w[sw]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const uint32_t acc_empty_leader0 = map_to_rank(&acc_empty[0], 0);
+    uint32_t it = 0;
+    for (int tile = cid; tile < n_total; tile += ncl, ++it) {
+      const uint32_t buf = it & 1;
+      const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], (it >> 1) & 1, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      const int m = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + row;
+      const int nt = tile % n_tiles;
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
+      if (EPI == kEpiGeGLU) {
+#pragma unroll 1
+        for (int c = 0; c < kHalfN; c += 32) {
+          float g[32], u[32];
+          tmem_ld_32x32b_x32(tb + c, g);
+          tmem_ld_32x32b_x32(tb + kHalfN + c, u);
+          if (m < p.M) {
+            __half* out = reinterpret_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + nt * kHalfN + c;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 o;
+              o.x = pack_f16x2_sat(gelu_tanh2(g[i]) * u[i], gelu_tanh2(g[i + 1]) * u[i + 1]);
+              o.y = pack_f16x2_sat(gelu_tanh2(g[i + 2]) * u[i + 2], gelu_tanh2(g[i + 3]) * u[i + 3]);
+              o.z = pack_f16x2_sat(gelu_tanh2(g[i + 4]) * u[i + 4], gelu_tanh2(g[i + 5]) * u[i + 5]);
+              o.w = pack_f16x2_sat(gelu_tanh2(g[i + 6]) * u[i + 6], gelu_tanh2(g[i + 7]) * u[i + 7]);
+              *reinterpret_cast<uint4*>(out + i) = o;
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 32) {
+          float v[32];
+          tmem_ld_32x32b_x32(tb + c, v);
+          if (m < p.M) {
+            const size_t off = static_cast<size_t>(m) * p.ldo + nt * kBN + c;
+            if (EPI == kEpiF16) {
+              __half* out = reinterpret_cast<__half*>(p.out) + off;
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                uint4 o;
+                o.x = pack_f16x2_sat(v[i], v[i + 1]);
+                o.y = pack_f16x2_sat(v[i + 2], v[i + 3]);
+                o.z = pack_f16x2_sat(v[i + 4], v[i + 5]);
+                o.w = pack_f16x2_sat(v[i + 6], v[i + 7]);
+                *reinterpret_cast<uint4*>(out + i) = o;
+              }
+            } else if (EPI == kEpiF32) {
+              float* out = reinterpret_cast<float*>(p.out) + off;
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            } else {  // kEpiResid
+              float* out = reinterpret_cast<float*>(p.out) + off;
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) {
+                float4 x = *reinterpret_cast<const float4*>(out + i);
+                x.x += v[i];
+                x.y += v[i + 1];
+                x.z += v[i + 2];
+                x.w += v[i + 3];
+                *reinterpret_cast<float4*>(out + i) = x;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty_leader0 + buf * 8);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+template <int EPI>
+cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const GemmParams& p,
+                   int num_sms, cudaStream_t st) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm2_q4k_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = ((p.M + kBM - 1) / kBM) * (p.N / kBN);
+  const int clusters = std::max(1, std::min(tiles, num_sms / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm2_q4k_kernel<EPI>, a, w0, w1, p);
+}
+
+}  // namespace
+
+bool gemm2_q4k_supports(int epi, int M, int N, int K) {
+  return (epi == kEpiF16 || epi == kEpiGeGLU || epi == kEpiResid || epi == kEpiF32) && M >= 1 && N % kBN == 0 &&
+         K % 256 == 0 && K >= 256;
+}
+
+cudaError_t gemm2_q4k_launch(int epi, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
+                             const GemmParams& p, int num_sms, cudaStream_t st) {
+  switch (epi) {
+    case kEpiF16: return launch<kEpiF16>(a, w0, w1, p, num_sms, st);
+    case kEpiGeGLU: return launch<kEpiGeGLU>(a, w0, w1, p, num_sms, st);
+    case kEpiResid: return launch<kEpiResid>(a, w0, w1, p, num_sms, st);
+    case kEpiF32: return launch<kEpiF32>(a, w0, w1, p, num_sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace wc

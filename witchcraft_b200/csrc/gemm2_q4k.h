@@ -1,0 +1,19 @@
+// Host-visible declarations of the 2-SM (cta_group::2) persistent Q4_K GEMM.
+#pragma once
+#include "gemm_q4k.h"
+
+namespace wc {
+
+// Rows of W one TMA box covers in the 2-SM kernel (each CTA's half of a
+// 256-column tile); its raw-weight tensor maps are encoded with this height.
+constexpr int kGemm2WBoxRows = 128;
+
+// True when the 2-SM kernel handles this epilogue and shape (N % 256 == 0,
+// K % 256 == 0; N is tile-space: 2 x features for kEpiGeGLU).
+bool gemm2_q4k_supports(int epi, int M, int N, int K);
+
+// Persistent launch over min(tiles, num_sms / 2) clusters of 2 CTAs.
+cudaError_t gemm2_q4k_launch(int epi, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
+                             const GemmParams& p, int num_sms, cudaStream_t st);
+
+}  // namespace wc

@@ -30,6 +30,7 @@
 #include "attention.h"
 #include "common.cuh"
 #include "elementwise.h"
+#include "gemm2_q4k.h"
 #include "gemm_q4k.h"
 #include "t5_host.h"
 
@@ -89,8 +90,23 @@ bool make_q4k_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K, ui
 struct LayerW {
   uint8_t *qkv, *o, *wi0, *wi1, *wo;
   float *ln0, *ln1;
-  CUtensorMap tm_qkv, tm_o, tm_wi0, tm_wi1, tm_wo;
+  CUtensorMap tm_qkv, tm_o, tm_wi0, tm_wi1, tm_wo;       // 1-SM kernel boxes
+  CUtensorMap tm2_qkv, tm2_o, tm2_wi0, tm2_wi1, tm2_wo;  // 2-SM kernel boxes
 };
+
+// Rows from which the 2-SM persistent GEMM replaces the 1-SM kernel.
+constexpr int kGemm2MinRows = 512;
+
+int device_sm_count(int dev) {
+  static int counts[64] = {};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 2) n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
 
 }  // namespace
 
@@ -207,6 +223,24 @@ int gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0,
   return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
 }
 
+// Layer GEMM: the 2-SM persistent kernel for large M, else the 1-SM kernel.
+int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
+               const CUtensorMap& w0_2, const CUtensorMap& w1_2, int M, int N, int K, void* out, int ldo,
+               cudaStream_t st) {
+  if (M >= kGemm2MinRows && gemm2_q4k_supports(epi, M, N, K)) {
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.out = out;
+    p.ldo = ldo;
+    p.status = h->d_status;
+    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, p, device_sm_count(h->device), st);
+    return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
+  }
+  return gemm(h, epi, bn, a, w0, w1, M, N, K, out, ldo, st);
+}
+
 int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, int L, float* out, float* norms,
                    float* outn, cudaStream_t st) {
   const T5Config& c = h->cfg;
@@ -219,15 +253,15 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, M, 3 * I, D, h->qkv, 3 * I, st)))
+    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, h->qkv, 3 * I, st)))
       return rc;
     if ((e = attention_launch(h->qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = gemm(h, kEpiResid, h->bn_o, h->tm_att, w.tm_o, w.tm_o, M, D, I, h->x, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiResid, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, h->x, D, st))) return rc;
     if ((e = rmsnorm_launch(h->x, w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
-    if ((rc = gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, M, 2 * F, D, h->hbuf, F, st))) return rc;
-    if ((rc = gemm(h, kEpiResid, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, M, D, F, h->x, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, h->hbuf, F, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiResid, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, h->x, D, st))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(h->x, next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
@@ -477,7 +511,12 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
          make_q4k_map(&w.tm_o, w.o, D, I, gemm_q4k_w_box_rows(kEpiResid, h->bn_o)) &&
          make_q4k_map(&w.tm_wi0, w.wi0, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
          make_q4k_map(&w.tm_wi1, w.wi1, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
-         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiResid, h->bn_wo));
+         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiResid, h->bn_wo)) &&
+         make_q4k_map(&w.tm2_qkv, w.qkv, 3 * I, D, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tm2_o, w.o, D, I, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tm2_wi0, w.wi0, F, D, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tm2_wi1, w.wi1, F, D, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tm2_wo, w.wo, D, F, kGemm2WBoxRows);
   }
   if (!ok) {
     wc_t5_destroy(h);
@@ -589,6 +628,26 @@ extern "C" int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const
   if (epilogue < 0 || epilogue > 3) return WC_E_INVALID_ARG;
   if (epilogue == kEpiGeGLU && !d_w_up) return WC_E_INVALID_ARG;
   const int tile_n = epilogue == kEpiGeGLU ? 2 * N : N;
+  if (M >= kGemm2MinRows && gemm2_q4k_supports(epilogue, M, tile_n, K)) {
+    CUtensorMap ta, tw0, tw1;
+    if (!make_act_map(&ta, d_x, M, K) || !make_q4k_map(&tw0, d_w, N, K, kGemm2WBoxRows) ||
+        !make_q4k_map(&tw1, epilogue == kEpiGeGLU ? d_w_up : d_w, N, K, kGemm2WBoxRows))
+      return WC_E_CUDA;
+    GemmParams p{};
+    p.M = M;
+    p.N = tile_n;
+    p.K = K;
+    p.out = d_out;
+    p.ldo = N;
+    p.status = kernel_status_word();
+    if (!p.status) return WC_E_CUDA;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return gemm2_q4k_launch(epilogue, ta, tw0, tw1, p, device_sm_count(dev), static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? WC_OK
+               : WC_E_CUDA;
+  }
   const int bn = gemm_q4k_bn_for(epilogue, tile_n);
   if (bn < 0) return WC_E_UNSUPPORTED;
   const int box = gemm_q4k_w_box_rows(epilogue, bn);
@@ -697,13 +756,13 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, M, 3 * I, D, qkv, 3 * I, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, qkv, 3 * I, st))) return rc;
     if ((e = attention_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = gemm(h, kEpiResid, h->bn_o, tm_att, w.tm_o, w.tm_o, M, D, I, x, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiResid, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, x, D, st))) return rc;
     if ((e = rmsnorm_launch(x, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
-    if ((rc = gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, M, 2 * F, D, hbuf, F, st))) return rc;
-    if ((rc = gemm(h, kEpiResid, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, M, D, F, x, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, hbuf, F, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiResid, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, x, D, st))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(x, next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
   }
