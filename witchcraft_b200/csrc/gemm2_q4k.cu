@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty_a = full_a + kSA;        // [kSA]  each CTA: MMA done with the stage
   uint64_t* full_w = empty_a + kSA;        // [kSW]  local raw Q4_K landed
   uint64_t* empty_w = full_w + kSW;        // [kSW]  local dequant warps done with it
-  uint64_t* full_b = empty_w + kSW;        // [kSB]  even CTA: 16 dequant warps of both CTAs
+  uint64_t* full_b = empty_w + kSW;        // [kSB]  even CTA: the owning warp pair of both CTAs
   uint64_t* empty_b = full_b + kSB;        // [kSB]  each CTA: MMA done with the stage
   uint64_t* acc_full = empty_b + kSB;      // [2]    each CTA: accumulator ready
   uint64_t* acc_empty = acc_full + 2;      // [2]    even CTA: 8 epilogue warps drained it
@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty_w[i], kDequantWarps);
     }
     for (int i = 0; i < kSB; ++i) {
-      mbar_init(&full_b[i], 2 * kDequantWarps);
+      mbar_init(&full_b[i], 4);  // 2 warps of the owning pair x 2 CTAs
       mbar_init(&empty_b[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -306,41 +306,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 2 + kDequantWarps) {
     // ------------------------------------------------------------ dequant
-    const int td = threadIdx.x - 64;   // 0..255
-    const int r = td & (kHalfN - 1);   // weight row within this CTA's half
-    const int hs = td >> 7;            // low (0) / high (1) nibble: sub-block 2ks + hs
-    const uint32_t full_b_leader0 = map_to_rank(&full_b[0], 0);
-    uint32_t iw = 0, ib = 0;
+    // The 4 B stages rotate over 4 pairs of warps: pair g dequantises every
+    // K step with (step % 4) == g, i.e. the 64-wide slice g of each Q4_K
+    // super-block, for all 128 weight rows of this CTA.  While one pair
+    // fences and signals its stage the other pairs keep converting.
+    static_assert(kSB == 4, "one B stage per dequant warp pair");
+    const int g = (warp - 2) >> 1;        // 0..3: slice of the super-block
+    const int gt = threadIdx.x - 64 - 64 * g;  // 0..63 within the pair
+    const uint32_t full_b_leader = map_to_rank(&full_b[g], 0);
+    uint8_t* bt = sB + g * kBBytes;
+    uint32_t iw = 0;
     bool ok = true;
     for (int tile = cid; tile < n_total && ok; tile += ncl) {
       for (int kb = 0; kb < kblocks && ok; ++kb, ++iw) {
         const uint32_t sw = iw % kSW;
         if (!(ok = mbar_wait(&full_w[sw], (iw / kSW) & 1, p.status))) break;
-        const uint8_t* blk = sW + sw * kWBytes + r * 144;
-        const Q4KScales sc = q4k_load_scales(blk);
+        if (!(ok = mbar_wait(&empty_b[g], (iw & 1) ^ 1, p.status))) break;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks, ++ib) {
-          const uint32_t sb = ib % kSB;
-          if (!(ok = mbar_wait(&empty_b[sb], ((ib / kSB) & 1) ^ 1, p.status))) break;
-          float d1f, m1f;
-          q4k_sub_scale(sc, 2 * ks + hs, d1f, m1f);
-          const uint64_t d1 = f2(d1f, d1f), negm1 = f2(-m1f, -m1f);
-          const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * ks);
+        for (int rr = 0; rr < 2; ++rr) {
+          const int r = gt + 64 * rr;
+          const uint8_t* blk = sW + sw * kWBytes + r * 144;
+          const Q4KScales sc = q4k_load_scales(blk);
+          const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
           const uint4 q0 = qp[0], q1 = qp[1];
           const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-          uint8_t* bt = sB + sb * kBBytes;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const uint32_t x0 = (qw[2 * cc] >> (4 * hs)) & 0x0F0F0F0Fu;
-            const uint32_t x1 = (qw[2 * cc + 1] >> (4 * hs)) & 0x0F0F0F0Fu;
-            *reinterpret_cast<uint4*>(bt + sw128_offset(r, hs * 4 + cc)) = dequant8_f16(x0, x1, d1, negm1);
+          for (int hs = 0; hs < 2; ++hs) {
+            float d1f, m1f;
+            q4k_sub_scale(sc, 2 * g + hs, d1f, m1f);
+            const uint64_t d1 = f2(d1f, d1f), negm1 = f2(-m1f, -m1f);
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              const uint32_t x0 = (qw[2 * cc] >> (4 * hs)) & 0x0F0F0F0Fu;
+              const uint32_t x1 = (qw[2 * cc + 1] >> (4 * hs)) & 0x0F0F0F0Fu;
+              *reinterpret_cast<uint4*>(bt + sw128_offset(r, hs * 4 + cc)) = dequant8_f16(x0, x1, d1, negm1);
+            }
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_remote(full_b_leader0 + sb * 8);
         }
+        fence_proxy_async_smem();
         __syncwarp();
-        if (ok && lane == 0) mbar_arrive(&empty_w[sw]);
+        if (lane == 0) {
+          mbar_arrive(&empty_w[sw]);
+          mbar_arrive_remote(full_b_leader);
+        }
       }
     }
   } else {
