@@ -57,7 +57,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
         o = os.path.join(BUILD_DIR, src + ".o")
         objs.append(o)
         if force or _stale(o, [s] + headers):
-            out = _run([nvcc, *ARCH, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
+            extra = os.environ.get("WC_EXTRA_NVCC_FLAGS", "").split()
+            out = _run([nvcc, *ARCH, *extra, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
                         "--expt-relaxed-constexpr", "-c", s, "-o", o])
             if verbose:
                 print(out)

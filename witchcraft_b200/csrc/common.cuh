@@ -173,6 +173,19 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
+// Hardware tanh (MUFU tanh.approx.f32, relative error about 2^-11, the size of
+// one f16 rounding of the output it feeds).
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// GELU, tanh form (candle's NewGelu / HF gelu_new, the XTR "gated-gelu"
+// activation): 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))).
+__device__ __forceinline__ float gelu_tanh_fast(float g) {
+  return 0.5f * g * (1.0f + tanh_fast(0.7978845608f * (g + 0.044715f * g * g * g)));
+}
+
 // Two f32 -> packed f16x2, round to nearest even.
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   __half2 v = __floats2half2_rn(lo, hi);

@@ -79,20 +79,31 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
   }
 }
 
-// lane owns float4 groups lane + 32*i, i < D/128
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+// lane owns float4 groups lane + 32*i, i < D/128.  With delta != null the
+// residual add of the preceding sub-layer happens here first: x += delta
+// (written back), then the norm of the updated row.
+__global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                __half* __restrict__ y, int M, int D, float eps) {
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
   const int ng = D / 128;
-  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * D);
+  float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(m) * D);
+  const float4* dr = delta ? reinterpret_cast<const float4*>(delta + static_cast<size_t>(m) * D) : nullptr;
   float4 v[kMaxD / 128];
   float ss = 0.f;
 #pragma unroll
   for (int g = 0; g < kMaxD / 128; ++g) {
     if (g < ng) {
       v[g] = xr[lane + 32 * g];
+      if (dr) {
+        const float4 d = dr[lane + 32 * g];
+        v[g].x += d.x;
+        v[g].y += d.y;
+        v[g].z += d.z;
+        v[g].w += d.w;
+        xr[lane + 32 * g] = v[g];
+      }
       ss += v[g].x * v[g].x + v[g].y * v[g].y + v[g].z * v[g].z + v[g].w * v[g].w;
     }
   }
@@ -130,11 +141,11 @@ cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, cons
   return cudaGetLastError();
 }
 
-cudaError_t rmsnorm_launch(const float* x, const float* w, __half* y, int M, int D, float eps,
+cudaError_t rmsnorm_launch(float* x, const float* delta, const float* w, __half* y, int M, int D, float eps,
                            cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 128 != 0 || D > kMaxD) return cudaErrorInvalidValue;
-  rmsnorm_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, w, y, M, D, eps);
+  rmsnorm_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, delta, w, y, M, D, eps);
   return cudaGetLastError();
 }
 

@@ -15,8 +15,9 @@ cudaError_t q4k_dequant_launch(const uint8_t* blocks, int64_t nblocks, float* ou
 cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, const int32_t* lengths, int L, int M,
                                  int D, const float* w, float eps, float* x, __half* xn, cudaStream_t st);
 
-// y[m] = f16(x[m] / sqrt(mean(x[m]^2) + eps) * w), D % 128 == 0.
-cudaError_t rmsnorm_launch(const float* x, const float* w, __half* y, int M, int D, float eps,
+// With delta != null first x[m] += delta[m] (the residual add, written back);
+// then y[m] = f16(x[m] / sqrt(mean(x[m]^2) + eps) * w), D % 128 == 0.
+cudaError_t rmsnorm_launch(float* x, const float* delta, const float* w, __half* y, int M, int D, float eps,
                            cudaStream_t st);
 
 }  // namespace wc

@@ -18,11 +18,12 @@
 // the wi_1 rows of the same 128 features, so accumulator columns [0, 128) are
 // gate and [128, 256) are up for every row.
 //
-// Warp roles (448 threads per CTA):
+// Warp roles (576 threads per CTA):
 //   warp 0      TMA producer (X stages; raw Q4_K stages)
 //   warp 1      TMEM allocation; MMA issue (even CTA, one thread)
 //   warps 2-9   dequant: raw Q4_K -> f16 K-major 128-B-swizzled B stages
-//   warps 10-13 epilogue: tcgen05.ld -> registers -> global
+//   warps 10-17 epilogue: tcgen05.ld -> registers -> global (two warps per
+//               TMEM lane quarter, one per column half)
 // Cross-CTA signalling: X loads of both CTAs complete on the even CTA's
 // barrier; dequant and epilogue warps arrive on the even CTA's barriers
 // through shared::cluster addresses; MMA completion is committed to both
@@ -52,9 +53,13 @@ constexpr int kOffW = kOffA + kSA * kABytes;
 constexpr int kOffB = kOffW + kSW * kWBytes;
 constexpr int kOffBar = kOffB + kSB * kBBytes;
 constexpr int kSmem = 1024 + kOffBar + 512;
-constexpr int kThreads = 448;
+#ifndef WC_GEMM2_EPI_WARPS
+#define WC_GEMM2_EPI_WARPS 4
+#endif
+constexpr int kEpiWarps = WC_GEMM2_EPI_WARPS;  // multiple of 4
+constexpr int kEpiSplit = kEpiWarps / 4;       // column parts per TMEM lane quarter
+constexpr int kThreads = 64 + 256 + 32 * kEpiWarps;
 constexpr int kDequantWarps = 8;
-constexpr int kEpiWarps = 4;
 constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -186,10 +191,6 @@ __device__ __forceinline__ uint4 dequant8_f16(uint32_t x0, uint32_t x1, uint64_t
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-__device__ __forceinline__ float gelu_tanh2(float g) {
-  return 0.5f * g * (1.0f + tanhf(0.7978845608f * (g + 0.044715f * g * g * g)));
-}
-
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_q4k_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full_b = empty_w + kSW;        // [kSB]  even CTA: the owning warp pair of both CTAs
   uint64_t* empty_b = full_b + kSB;        // [kSB]  each CTA: MMA done with the stage
   uint64_t* acc_full = empty_b + kSB;      // [2]    each CTA: accumulator ready
-  uint64_t* acc_empty = acc_full + 2;      // [2]    even CTA: 8 epilogue warps drained it
+  uint64_t* acc_empty = acc_full + 2;      // [2]    even CTA: 16 epilogue warps drained it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5;
@@ -356,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
+    const int half = (warp - 10) >> 2;  // column part of the tile
     const int row = q * 32 + lane;
     const uint32_t acc_empty_leader0 = map_to_rank(&acc_empty[0], 0);
     uint32_t it = 0;
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
       if (EPI == kEpiGeGLU) {
 #pragma unroll 1
-        for (int c = 0; c < kHalfN; c += 32) {
+        for (int c = half * (kHalfN / kEpiSplit); c < (half + 1) * (kHalfN / kEpiSplit); c += 32) {
           float g[32], u[32];
           tmem_ld_32x32b_x32(tb + c, g);
           tmem_ld_32x32b_x32(tb + kHalfN + c, u);
@@ -379,17 +381,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
               uint4 o;
-              o.x = pack_f16x2_sat(gelu_tanh2(g[i]) * u[i], gelu_tanh2(g[i + 1]) * u[i + 1]);
-              o.y = pack_f16x2_sat(gelu_tanh2(g[i + 2]) * u[i + 2], gelu_tanh2(g[i + 3]) * u[i + 3]);
-              o.z = pack_f16x2_sat(gelu_tanh2(g[i + 4]) * u[i + 4], gelu_tanh2(g[i + 5]) * u[i + 5]);
-              o.w = pack_f16x2_sat(gelu_tanh2(g[i + 6]) * u[i + 6], gelu_tanh2(g[i + 7]) * u[i + 7]);
+              o.x = pack_f16x2_sat(gelu_tanh_fast(g[i]) * u[i], gelu_tanh_fast(g[i + 1]) * u[i + 1]);
+              o.y = pack_f16x2_sat(gelu_tanh_fast(g[i + 2]) * u[i + 2], gelu_tanh_fast(g[i + 3]) * u[i + 3]);
+              o.z = pack_f16x2_sat(gelu_tanh_fast(g[i + 4]) * u[i + 4], gelu_tanh_fast(g[i + 5]) * u[i + 5]);
+              o.w = pack_f16x2_sat(gelu_tanh_fast(g[i + 6]) * u[i + 6], gelu_tanh_fast(g[i + 7]) * u[i + 7]);
               *reinterpret_cast<uint4*>(out + i) = o;
             }
           }
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < kBN; c += 32) {
+        for (int c = half * (kBN / kEpiSplit); c < (half + 1) * (kBN / kEpiSplit); c += 32) {
           float v[32];
           tmem_ld_32x32b_x32(tb + c, v);
           if (m < p.M) {

@@ -51,10 +51,6 @@ struct GemmCfg {
   static_assert(W_BYTES % 1024 == 0, "raw stage must keep 1024-B alignment");
 };
 
-__device__ __forceinline__ float gelu_tanh(float g) {
-  return 0.5f * g * (1.0f + tanhf(0.7978845608f * (g + 0.044715f * g * g * g)));
-}
-
 template <int BN, int EPI>
 __global__ void __launch_bounds__(320, 1)
     gemm_q4k_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
@@ -271,10 +267,10 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
               uint4 o;
-              o.x = pack_f16x2_sat(gelu_tanh(g[i]) * u[i], gelu_tanh(g[i + 1]) * u[i + 1]);
-              o.y = pack_f16x2_sat(gelu_tanh(g[i + 2]) * u[i + 2], gelu_tanh(g[i + 3]) * u[i + 3]);
-              o.z = pack_f16x2_sat(gelu_tanh(g[i + 4]) * u[i + 4], gelu_tanh(g[i + 5]) * u[i + 5]);
-              o.w = pack_f16x2_sat(gelu_tanh(g[i + 6]) * u[i + 6], gelu_tanh(g[i + 7]) * u[i + 7]);
+              o.x = pack_f16x2_sat(gelu_tanh_fast(g[i]) * u[i], gelu_tanh_fast(g[i + 1]) * u[i + 1]);
+              o.y = pack_f16x2_sat(gelu_tanh_fast(g[i + 2]) * u[i + 2], gelu_tanh_fast(g[i + 3]) * u[i + 3]);
+              o.z = pack_f16x2_sat(gelu_tanh_fast(g[i + 4]) * u[i + 4], gelu_tanh_fast(g[i + 5]) * u[i + 5]);
+              o.w = pack_f16x2_sat(gelu_tanh_fast(g[i + 6]) * u[i + 6], gelu_tanh_fast(g[i + 7]) * u[i + 7]);
               *reinterpret_cast<uint4*>(out + i) = o;
             }
           }

@@ -6,11 +6,11 @@
 //   per layer l:
 //     gemm  kEpiF16   qkv = xn . [Wq|Wk|Wv]^T                (f16 [M][3*inner])
 //     attention        att = softmax(QK^T + bias, key mask) V (f16 [M][inner])
-//     gemm  kEpiResid  x += att . Wo^T                        (f32)
-//     rmsnorm          xn = RMSNorm_ff(x)
+//     gemm  kEpiF32    y = att . Wo^T   (f32, into the dead qkv buffer)
+//     rmsnorm          x += y; xn = RMSNorm_ff(x)
 //     gemm  kEpiGeGLU  h = gelu(xn . Wi0^T) * (xn . Wi1^T)    (f16 [M][d_ff])
-//     gemm  kEpiResid  x += h . Wwo^T
-//     rmsnorm          xn = RMSNorm_{next attn | final}(x)
+//     gemm  kEpiF32    y = h . Wwo^T
+//     rmsnorm          x += y; xn = RMSNorm_{next attn | final}(x)
 //   gemm  kEpiProj     out = xn . Wlin^T, norms, out / norm   (f32 [M][128])
 // following T5Stack::forward / T5Block::forward / T5EncoderModel::forward
 // (src/quantized_t5.rs:654-670, 598-628, 698-701).  The residual stream x
@@ -174,7 +174,7 @@ int ensure_workspace(wc_t5* h, int64_t rows, int B) {
   size_t off = 0;
   const size_t o_x = off; off = align256(off + cap * D * 4);
   const size_t o_xn = off; off = align256(off + cap * D * 2);
-  const size_t o_qkv = off; off = align256(off + cap * 3 * I * 2);
+  const size_t o_qkv = off; off = align256(off + cap * std::max(3 * I * 2, D * 4));  // also the f32 O / wo output
   const size_t o_att = off; off = align256(off + cap * I * 2);
   const size_t o_h = off; off = align256(off + cap * F * 2);
   const size_t o_ids = off; off = align256(off + cap * 4);
@@ -257,13 +257,13 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
       return rc;
     if ((e = attention_launch(h->qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, kEpiResid, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, h->x, D, st))) return rc;
-    if ((e = rmsnorm_launch(h->x, w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, h->qkv, D, st))) return rc;
+    if ((e = rmsnorm_launch(h->x, reinterpret_cast<const float*>(h->qkv), w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
     if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, h->hbuf, F, st))) return rc;
-    if ((rc = layer_gemm(h, kEpiResid, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, h->x, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, h->qkv, D, st))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
-    if ((e = rmsnorm_launch(h->x, next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
+    if ((e = rmsnorm_launch(h->x, reinterpret_cast<const float*>(h->qkv), next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
   }
   return gemm(h, kEpiProj, 128, h->tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
@@ -489,9 +489,9 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
   h->rel_bias = reinterpret_cast<float*>(h->arena + o_bias);
   h->bt = t5_bucket_thresholds(cfg.num_buckets, cfg.max_distance, kMaxL);
   h->bn_qkv = gemm_q4k_bn_for(kEpiF16, 3 * I);
-  h->bn_o = gemm_q4k_bn_for(kEpiResid, D);
+  h->bn_o = gemm_q4k_bn_for(kEpiF32, D);
   h->bn_wi = gemm_q4k_bn_for(kEpiGeGLU, 2 * F);
-  h->bn_wo = gemm_q4k_bn_for(kEpiResid, D);
+  h->bn_wo = gemm_q4k_bn_for(kEpiF32, D);
   if (h->bn_qkv < 0 || h->bn_o < 0 || h->bn_wi < 0 || h->bn_wo < 0) {
     wc_t5_destroy(h);
     return fail(nullptr, WC_E_UNSUPPORTED, "no GEMM tiling for these model dimensions");
@@ -508,10 +508,10 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
     w.ln0 = reinterpret_cast<float*>(h->arena + lo[l].ln0);
     w.ln1 = reinterpret_cast<float*>(h->arena + lo[l].ln1);
     ok = make_q4k_map(&w.tm_qkv, w.qkv, 3 * I, D, gemm_q4k_w_box_rows(kEpiF16, h->bn_qkv)) &&
-         make_q4k_map(&w.tm_o, w.o, D, I, gemm_q4k_w_box_rows(kEpiResid, h->bn_o)) &&
+         make_q4k_map(&w.tm_o, w.o, D, I, gemm_q4k_w_box_rows(kEpiF32, h->bn_o)) &&
          make_q4k_map(&w.tm_wi0, w.wi0, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
          make_q4k_map(&w.tm_wi1, w.wi1, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
-         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiResid, h->bn_wo)) &&
+         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiF32, h->bn_wo)) &&
          make_q4k_map(&w.tm2_qkv, w.qkv, 3 * I, D, kGemm2WBoxRows) &&
          make_q4k_map(&w.tm2_o, w.o, D, I, kGemm2WBoxRows) &&
          make_q4k_map(&w.tm2_wi0, w.wi0, F, D, kGemm2WBoxRows) &&
@@ -713,7 +713,7 @@ NoAllocLayout noalloc_layout(const wc_t5* h, int64_t M) {
   size_t off = 0;
   l.x = off; off = align256(off + M * D * 4);
   l.xn = off; off = align256(off + M * D * 2);
-  l.qkv = off; off = align256(off + M * 3 * I * 2);
+  l.qkv = off; off = align256(off + M * std::max(3 * I * 2, D * 4));  // also the f32 O / wo output
   l.att = off; off = align256(off + M * I * 2);
   l.h = off; off = align256(off + M * F * 2);
   l.total = off;
@@ -759,12 +759,12 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
     if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, qkv, 3 * I, st))) return rc;
     if ((e = attention_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, kEpiResid, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, x, D, st))) return rc;
-    if ((e = rmsnorm_launch(x, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, qkv, D, st))) return rc;
+    if ((e = rmsnorm_launch(x, reinterpret_cast<const float*>(qkv), w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
     if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, hbuf, F, st))) return rc;
-    if ((rc = layer_gemm(h, kEpiResid, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, x, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, qkv, D, st))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
-    if ((e = rmsnorm_launch(x, next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    if ((e = rmsnorm_launch(x, reinterpret_cast<const float*>(qkv), next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
   }
   return gemm(h, kEpiProj, 128, tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
               lengths, L);
