@@ -144,3 +144,18 @@ def test_two_handles_on_one_device(tiny_model):
     a.close()
     np.testing.assert_array_equal(b.forward(ids), b.forward(ids))
     b.close()
+
+
+def test_graph_replay_matches_eager(xtr_gpu, xtr_oracle):
+    """Small batches replay a captured CUDA graph from their second call on;
+    every call must still see its own inputs."""
+    rng = np.random.default_rng(12)
+    lengths = [32, 9]
+    runs = []
+    for i in range(4):
+        ids = rng.integers(3, 32128, (2, 32)).astype(np.uint32)
+        runs.append((ids, xtr_gpu.forward(ids, lengths)))
+    for ids, out in runs:
+        _check(out, xtr_oracle.encode(ids, lengths), lengths)
+    again = xtr_gpu.forward(runs[0][0], lengths)
+    np.testing.assert_array_equal(again, runs[0][1])

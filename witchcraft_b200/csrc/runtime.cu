@@ -19,7 +19,9 @@
 #include <cuda_runtime.h>
 #include <string.h>
 
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -138,6 +140,18 @@ struct wc_t5 {
   int32_t* d_len = nullptr;
   float *d_out = nullptr, *d_norms = nullptr, *d_outn = nullptr;
   uint32_t* d_status = nullptr;
+  // CUDA graphs of the kernel sequence for small batches, keyed by shape,
+  // buffers and stream; an entry first records that the key was seen and is
+  // captured on its second use.
+  struct GraphKey {
+    int B, L;
+    const void *ids, *len, *out, *norms, *outn;
+    cudaStream_t st;
+    bool operator<(const GraphKey& o) const {
+      return std::tie(B, L, ids, len, out, norms, outn, st) < std::tie(o.B, o.L, o.ids, o.len, o.out, o.norms, o.outn, o.st);
+    }
+  };
+  std::map<GraphKey, cudaGraphExec_t> graphs;  // nullptr = seen once, not captured
   std::string err;
 };
 
@@ -156,7 +170,14 @@ int cuda_fail(wc_t5* h, cudaError_t e, const char* what) {
   return fail(h, WC_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+void clear_graphs(wc_t5* h) {
+  for (auto& kv : h->graphs)
+    if (kv.second) cudaGraphExecDestroy(kv.second);
+  h->graphs.clear();
+}
+
 void free_workspace(wc_t5* h) {
+  clear_graphs(h);  // captured graphs hold workspace pointers
   if (h->ws) cudaFree(h->ws);
   h->ws = nullptr;
   h->cap_rows = 0;
@@ -278,6 +299,49 @@ int check_status(wc_t5* h, cudaStream_t st) {
   if (s & kStatusWaitTimeout) return fail(h, WC_E_TIMEOUT, "an in-kernel wait timed out");
   if (s) return fail(h, WC_E_CUDA, "kernel reported status " + std::to_string(s));
   return WC_OK;
+}
+
+// Batches up to this many rows replay a captured CUDA graph of the ~86
+// launches instead of launching them one by one (launch overhead dominates a
+// 32-token query).
+constexpr int64_t kGraphMaxRows = 4096;
+
+int forward_cached(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, int L, float* out, float* norms,
+                   float* outn, cudaStream_t st) {
+  const int64_t M = static_cast<int64_t>(B) * L;
+  if (M > kGraphMaxRows || st == nullptr || st == cudaStreamLegacy || st == cudaStreamPerThread)
+    return forward_device(h, ids, lengths, B, L, out, norms, outn, st);
+  const wc_t5::GraphKey key{B, L, ids, lengths, out, norms, outn, st};
+  auto it = h->graphs.find(key);
+  if (it != h->graphs.end() && it->second) {
+    cudaError_t e = cudaGraphLaunch(it->second, st);
+    return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "graph launch");
+  }
+  if (it == h->graphs.end()) {
+    if (h->graphs.size() >= 256) clear_graphs(h);
+    h->graphs[key] = nullptr;  // seen once: run eagerly
+    return forward_device(h, ids, lengths, B, L, out, norms, outn, st);
+  }
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return cuda_fail(h, e, "graph capture begin");
+  const int rc = forward_device(h, ids, lengths, B, L, out, norms, outn, st);
+  e = cudaStreamEndCapture(st, &graph);
+  if (rc != WC_OK || e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    h->graphs.erase(key);
+    return rc != WC_OK ? rc : cuda_fail(h, e, "graph capture");
+  }
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    h->graphs.erase(key);
+    return cuda_fail(h, e, "graph instantiate");
+  }
+  h->graphs[key] = exec;
+  e = cudaGraphLaunch(exec, st);
+  return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "graph launch");
 }
 
 struct DeviceGuard {
@@ -546,7 +610,7 @@ extern "C" int wc_t5_forward_device(wc_t5* h, const uint32_t* d_ids, const int32
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(h->d_status, 0, 4, st);
   if (e != cudaSuccess) return cuda_fail(h, e, "status reset");
-  return forward_device(h, d_ids, d_lengths, B, L, d_out, d_norms, d_outn, st);
+  return forward_cached(h, d_ids, d_lengths, B, L, d_out, d_norms, d_outn, st);
 }
 
 extern "C" int wc_t5_sync(wc_t5* h, void* stream) {
@@ -583,7 +647,7 @@ extern "C" int wc_t5_forward(wc_t5* h, const uint32_t* ids, const int32_t* lengt
       (e = cudaMemcpyAsync(h->d_ids, ids, M * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
       (e = cudaMemcpyAsync(h->d_len, len.data(), B * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
     return cuda_fail(h, e, "input upload");
-  rc = forward_device(h, h->d_ids, h->d_len, B, L, h->d_out, norms ? h->d_norms : nullptr,
+  rc = forward_cached(h, h->d_ids, h->d_len, B, L, h->d_out, norms ? h->d_norms : nullptr,
                       out_normalised ? h->d_outn : nullptr, st);
   if (rc) return rc;
   const size_t ob = static_cast<size_t>(M) * h->d_proj * 4;
