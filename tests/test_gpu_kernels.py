@@ -46,10 +46,12 @@ def _weights(N, K, seed):
     return blocks, wd
 
 
-# M >= 512 with N % 256 == 0 runs the 2-SM persistent kernel, the rest the 1-SM kernel
+# M <= 32 runs the small-M kernel (except the residual epilogue), M >= 512 with N % 256 == 0 the
+# 2-SM persistent kernel, the rest the 1-SM kernel
 @pytest.mark.parametrize("M,K,N", [(8192, 768, 2304), (8192, 2048, 768), (1, 768, 768), (77, 768, 2304),
                                    (300, 2048, 768), (129, 256, 128), (2048, 768, 128), (511, 768, 768),
-                                   (512, 768, 768), (1000, 2048, 768), (16384, 768, 256), (700, 256, 512)])
+                                   (512, 768, 768), (1000, 2048, 768), (16384, 768, 256), (700, 256, 512),
+                                   (5, 2048, 768), (16, 768, 2304), (32, 2048, 768), (9, 256, 128), (33, 768, 768)])
 @pytest.mark.parametrize("epi", [0, 3])
 def test_gemm_store(M, K, N, epi):
     blocks, wd = _weights(N, K, seed=M + N)
@@ -66,7 +68,8 @@ def test_gemm_store(M, K, N, epi):
 
 
 @pytest.mark.parametrize("M,K,F", [(8192, 768, 2048), (200, 768, 2048), (64, 256, 512), (1300, 768, 2048),
-                                   (600, 256, 512)])
+                                   (600, 256, 512),
+                                   (1, 768, 2048), (13, 768, 2048), (32, 256, 512)])
 def test_gemm_geglu(M, K, F):
     b0, w0 = _weights(F, K, 10)
     b1, w1 = _weights(F, K, 11)

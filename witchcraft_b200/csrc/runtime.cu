@@ -34,6 +34,7 @@
 #include "elementwise.h"
 #include "gemm2_q4k.h"
 #include "gemm_q4k.h"
+#include "gemv_q4k.h"
 #include "t5_host.h"
 
 namespace wc {
@@ -245,9 +246,16 @@ int gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0,
 }
 
 // Layer GEMM: the 2-SM persistent kernel for large M, else the 1-SM kernel.
+// Up to kGemvMaxRows rows the small-M kernel (all SMs stream the weights once)
+// runs instead; it reads the activations and the raw weights by pointer.
 int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
                const CUtensorMap& w0_2, const CUtensorMap& w1_2, int M, int N, int K, void* out, int ldo,
-               cudaStream_t st) {
+               cudaStream_t st, const __half* a_ptr, const uint8_t* w0_ptr, const uint8_t* w1_ptr) {
+  const int feat = epi == kEpiGeGLU ? N / 2 : N;
+  if (gemv_q4k_supports(epi, M, feat, K)) {
+    cudaError_t e = gemv_q4k_launch(epi, a_ptr, M, K, w0_ptr, w1_ptr, feat, out, ldo, st);
+    return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
+  }
   if (M >= kGemm2MinRows && gemm2_q4k_supports(epi, M, N, K)) {
     GemmParams p{};
     p.M = M;
@@ -274,15 +282,15 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, h->qkv, 3 * I, st)))
+    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, h->qkv, 3 * I, st, h->xn, w.qkv, w.qkv)))
       return rc;
     if ((e = attention_launch(h->qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, h->qkv, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, h->qkv, D, st, h->att, w.o, w.o))) return rc;
     if ((e = rmsnorm_launch(h->x, reinterpret_cast<const float*>(h->qkv), w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
-    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, h->hbuf, F, st))) return rc;
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, h->qkv, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, h->hbuf, F, st, h->xn, w.wi0, w.wi1))) return rc;
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, h->qkv, D, st, h->hbuf, w.wo, w.wo))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(h->x, reinterpret_cast<const float*>(h->qkv), next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
@@ -692,6 +700,12 @@ extern "C" int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const
   if (epilogue < 0 || epilogue > 3) return WC_E_INVALID_ARG;
   if (epilogue == kEpiGeGLU && !d_w_up) return WC_E_INVALID_ARG;
   const int tile_n = epilogue == kEpiGeGLU ? 2 * N : N;
+  if (gemv_q4k_supports(epilogue, M, N, K))
+    return gemv_q4k_launch(epilogue, static_cast<const __half*>(d_x), M, K, static_cast<const uint8_t*>(d_w),
+                           static_cast<const uint8_t*>(epilogue == kEpiGeGLU ? d_w_up : d_w), N, d_out, N,
+                           static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? WC_OK
+               : WC_E_CUDA;
   if (M >= kGemm2MinRows && gemm2_q4k_supports(epilogue, M, tile_n, K)) {
     CUtensorMap ta, tw0, tw1;
     if (!make_act_map(&ta, d_x, M, K) || !make_q4k_map(&tw0, d_w, N, K, kGemm2WBoxRows) ||
@@ -820,13 +834,13 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, qkv, 3 * I, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
     if ((e = attention_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, qkv, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, qkv, D, st, att, w.o, w.o))) return rc;
     if ((e = rmsnorm_launch(x, reinterpret_cast<const float*>(qkv), w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
-    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, hbuf, F, st))) return rc;
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, qkv, D, st))) return rc;
+    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
+    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, qkv, D, st, hbuf, w.wo, w.wo))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(x, reinterpret_cast<const float*>(qkv), next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
   }
