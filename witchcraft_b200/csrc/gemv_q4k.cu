@@ -5,7 +5,8 @@
 // weight is dequantised exactly once.  One CTA owns 16 weight rows (output
 // features) -- for the gated GELU 16 wi_0 rows and the same 16 wi_1 rows --
 // and all M tokens; its 4 warps split K by Q4_K super-block.  A warp copies
-// the raw super-blocks of its rows to shared memory, dequantises them straight
+// (cp.async, all at once) the raw super-blocks of its rows to shared memory,
+// dequantises them straight
 // into the A-operand registers of mma.sync m16n8k16 (weights x tokens, f16 in,
 // f32 accumulate; the activations, staged once per CTA in shared memory, are
 // the B operand), and the 4 warps' partial sums are added in shared memory
@@ -27,6 +28,11 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(pred ? 16 : 0)
+               : "memory");
+}
+
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -54,21 +60,33 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q4k_kernel(const __half* __r
   extern __shared__ __align__(16) uint8_t smem[];
   const int xstride = K * 2 + 16;  // bytes per token row (padded: conflict-free ldmatrix)
   uint8_t* sX = smem;
-  uint8_t* sW = smem + TOK * xstride;                               // [warp][NMAT*16 rows][144]
-  float* sRed = reinterpret_cast<float*>(sW + kWarps * NMAT * kRows * 144);  // [warp][NMAT][16][TOK]
+  uint8_t* sW = smem + TOK * xstride;  // [warp][its super-blocks][NMAT*16 rows][144]
+  float* sRed = reinterpret_cast<float*>(sW + ((K / 256 + kWarps - 1) / kWarps) * kWarps * NMAT * kRows * 144);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = blockIdx.x * kRows;
   const int kblocks = K / 256;
   const size_t wrow_bytes = static_cast<size_t>(kblocks) * 144;
 
-  // activations: TOK rows (rows >= M are zero) x K f16
+  // Everything this CTA reads is requested up front with cp.async (the
+  // activations, TOK rows with rows >= M zero-filled, and every raw
+  // super-block of this warp's rows), then waited for once.
+  const int kb_per_warp = (kblocks + kWarps - 1) / kWarps;
+  uint8_t* myW = sW + warp * kb_per_warp * NMAT * kRows * 144;
   for (int i = tid; i < TOK * (K / 8); i += blockDim.x) {
     const int r = i / (K / 8), c = i % (K / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < M) v = *reinterpret_cast<const uint4*>(X + static_cast<size_t>(r) * K + c * 8);
-    *reinterpret_cast<uint4*>(sX + r * xstride + c * 16) = v;
+    cp_async16(sX + r * xstride + c * 16, X + static_cast<size_t>(r < M ? r : 0) * K + c * 8, r < M);
   }
+  for (int s = 0; s < kb_per_warp; ++s) {
+    const int kb = warp + s * kWarps;
+    if (kb >= kblocks) break;
+    for (int i = lane; i < NMAT * kRows * 9; i += 32) {
+      const int rr = i / 9, c = i % 9;
+      const uint8_t* src = (rr < kRows ? W0 : W1) + (row0 + (rr % kRows)) * wrow_bytes + kb * 144 + c * 16;
+      cp_async16(myW + (s * NMAT * kRows + rr) * 144 + c * 16, src, true);
+    }
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
   float acc[NMAT][MT][4];
@@ -77,20 +95,15 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q4k_kernel(const __half* __r
 #pragma unroll
     for (int t = 0; t < MT; ++t) acc[m][t][0] = acc[m][t][1] = acc[m][t][2] = acc[m][t][3] = 0.f;
 
-  uint8_t* myW = sW + warp * NMAT * kRows * 144;
   const int g = lane >> 2, tq = lane & 3;
-  for (int kb = warp; kb < kblocks; kb += kWarps) {
-    // raw super-blocks of this warp's rows -> smem (9 x 16 B per row)
-    for (int i = lane; i < NMAT * kRows * 9; i += 32) {
-      const int rr = i / 9, c = i % 9;
-      const uint8_t* src = (rr < kRows ? W0 : W1) + (row0 + (rr % kRows)) * wrow_bytes + kb * 144 + c * 16;
-      *reinterpret_cast<uint4*>(myW + rr * 144 + c * 16) = *reinterpret_cast<const uint4*>(src);
-    }
-    __syncwarp();
+  for (int s = 0; s < kb_per_warp; ++s) {
+    const int kb = warp + s * kWarps;
+    if (kb >= kblocks) break;
+    const uint8_t* wblk = myW + s * NMAT * kRows * 144;
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
-      const uint8_t* blkA = myW + (m * kRows + g) * 144;      // row g
-      const uint8_t* blkB = myW + (m * kRows + g + 8) * 144;  // row g + 8
+      const uint8_t* blkA = wblk + (m * kRows + g) * 144;      // row g
+      const uint8_t* blkB = wblk + (m * kRows + g + 8) * 144;  // row g + 8
       const Q4KScales sa = q4k_load_scales(blkA);
       const Q4KScales sb = q4k_load_scales(blkB);
 #pragma unroll
@@ -123,7 +136,6 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q4k_kernel(const __half* __r
         }
       }
     }
-    __syncwarp();
   }
 
   // partial sums of the 4 warps -> smem, then reduce + epilogue
@@ -164,7 +176,8 @@ template <int EPI, int MT>
 cudaError_t launch(const __half* X, int M, int K, const uint8_t* W0, const uint8_t* W1, int N, void* out, int ldo,
                    cudaStream_t st) {
   constexpr int NMAT = EPI == kEpiGeGLU ? 2 : 1;
-  const size_t smem = static_cast<size_t>(MT * 8) * (K * 2 + 16) + kWarps * NMAT * kRows * 144 +
+  const int kb_per_warp = (K / 256 + kWarps - 1) / kWarps;
+  const size_t smem = static_cast<size_t>(MT * 8) * (K * 2 + 16) + kb_per_warp * kWarps * NMAT * kRows * 144 +
                       kWarps * NMAT * kRows * MT * 8 * 4;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   static bool attr_set[64] = {};
