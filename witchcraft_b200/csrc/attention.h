@@ -1,5 +1,6 @@
-// Host-visible declarations of the encoder attention kernel.
+// Host-visible declarations of the encoder attention kernel (attention_tc.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -16,9 +17,9 @@ struct BucketThresholds {
   int thr[32];   // thr[v] = smallest distance d with bucket_half(d) >= v
 };
 
-// qkv: [B*L][3*H*64] f16 (q | k | v); out: [B*L][H*64] f16;
-// lengths: device [B]; bias_tab: device f32 [num_buckets][H].
-cudaError_t attention_launch(const __half* qkv, __half* out, const int32_t* lengths, int B, int L,
-                             int H, const float* bias_tab, const BucketThresholds& bt, cudaStream_t st);
+// tcgen05 attention: tm_qkv is the TMA descriptor of the QKV projection
+// [B*L][3*H*64] f16 (box 64 x 64, 128-byte swizzle); L <= 2048.
+cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const int32_t* lengths, int B, int L, int H,
+                                const float* bias_tab, const BucketThresholds& bt, uint32_t* status, cudaStream_t st);
 
 }  // namespace wc

@@ -1,0 +1,422 @@
+// Bidirectional T5 encoder self-attention on the 5th-generation tensor cores
+// (tcgen05 + TMEM), flash-style with an online softmax, the T5 relative-
+// position bias and a key padding mask.  Replaces src/quantized_t5.rs:426-500:
+// scores without 1/sqrt(d) scaling, + position bias, softmax_last_dim, P.V,
+// transpose back to tokens.
+//
+// One CTA owns 128 queries of one sequence for a group of heads and walks the
+// flattened sequence of steps (head, 64-key tile) as one pipeline, so the
+// TMA loads and S MMAs of the next step -- also across a head boundary --
+// overlap the softmax of the current one:
+//   warp 0      TMA: per head the Q tile, then its K and V tiles (two
+//               3-stage rings; a K stage is freed as soon as its S is done)
+//   warp 1      TMEM allocation and the single MMA-issuing thread
+//   warps 2-5   softmax and epilogue (thread = query row = TMEM lane)
+// Step t (head h, key tile j): S(t) = Q_h K_j^T (M=128, N=64, K=64, f32 in
+// TMEM buffer t % 2, computed ahead); the softmax warps add the relative-
+// position bias (a per-tile window of 191 biases they build), mask keys past
+// the sequence, update the running max / sum, rescale the O row of head h in
+// TMEM when the max moved and write P = 2^(S - max) as f16 into shared memory
+// (buffer t % 2, K-major, 128-B swizzle); then O_h += P V_j (M=128, N=64,
+// K=64; V read MN-major from its TMA tile).  O has two TMEM buffers
+// (head % 2), so the epilogue of one head overlaps the next head's steps.
+// Input: the token-major QKV projection [B*L][3*H*64] f16 through one TMA
+// descriptor (box 64 x 64); output [B*L][H*64] f16.  Query rows of an
+// all-padding tile are written as zeros.
+#include "attention.h"
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace wc {
+
+namespace {
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 columns without waiting; tmem_wait_ld() completes them.
+__device__ __forceinline__ void tmem_ld_32x32b_x32_nowait(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Shared-memory descriptor of an MN-major operand with the 128-byte swizzle:
+// rows of 64 f16 along N (128 B) for consecutive K, 8-row groups 1024 B apart
+// (stride byte offset); the leading byte offset (stride between 64-wide N
+// atoms) is unused for N = 64.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(8192u >> 4) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+__device__ __forceinline__ int rel_bucket_tc(const BucketThresholds& bt, int delta) {
+  const int d = delta < 0 ? -delta : delta;
+  int f = 0;
+#pragma unroll
+  for (int v = 1; v < 32; ++v) f += (v < bt.half && d >= bt.thr[v]) ? 1 : 0;  // constant indices: registers
+  return f + (delta > 0 ? bt.half : 0);
+}
+
+
+constexpr int kQ = 128;       // queries per CTA
+constexpr int kKeys = 64;     // keys per tile
+constexpr int kDh = 64;
+constexpr int kQBytes = kQ * 128;      // 128 x 64 f16
+constexpr int kKVBytes = kKeys * 128;  // 64 x 64 f16
+constexpr int kPBytes = kQ * 128;      // 128 x 64 f16 (one 64-wide swizzle atom)
+constexpr int kWin = kQ + kKeys - 1;   // distinct key - query offsets of one tile pair
+constexpr int kMaxHeads = 16;          // heads of one CTA's group
+constexpr int kKVStages = 3;
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kQBytes;                // kKVStages stages
+constexpr int kOffV = kOffK + kKVStages * kKVBytes;   // kKVStages stages
+constexpr int kOffP = kOffV + kKVStages * kKVBytes;   // 2 buffers
+constexpr int kOffWin = kOffP + 2 * kPBytes;  // f32 [2][kWin + 1]
+constexpr int kOffTab = kOffWin + 2 * (kWin + 1) * 4;  // f32 [kMaxHeads][64]
+constexpr int kOffBar = kOffTab + kMaxHeads * 64 * 4;
+constexpr int kSmem = 1024 + kOffBar + 256;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0, kColO = 128;  // S buffers at 0 / 64, O buffers at 128 / 192
+constexpr int kMaxL = 2048;
+
+__global__ void __launch_bounds__(kThreads)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __half* __restrict__ out,
+                        const int32_t* __restrict__ lengths, int L, int H, int heads_per_cta,
+                        const float* __restrict__ bias_tab, BucketThresholds bt, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + kOffQ;
+  uint8_t* sK = smem + kOffK;
+  uint8_t* sV = smem + kOffV;
+  uint8_t* sP = smem + kOffP;
+  float* sWin = reinterpret_cast<float*>(smem + kOffWin);
+  float* sTab = reinterpret_cast<float*>(smem + kOffTab);  // [head in group][bucket] * log2(e)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars;          // [1]
+  uint64_t* q_empty = bars + 1;     // [1]
+  uint64_t* k_full = bars + 2;      // [kKVStages]
+  uint64_t* k_empty = bars + 5;     // [kKVStages]  freed when S(t) is done
+  uint64_t* v_full = bars + 8;      // [kKVStages]
+  uint64_t* v_empty = bars + 11;    // [kKVStages]  freed when P(t) V(t) is done
+  uint64_t* s_full = bars + 14;     // [2] per S buffer
+  uint64_t* p_full = bars + 16;     // [1] (4 softmax warps arrive)
+  uint64_t* o_done = bars + 17;     // [1] one phase per step
+  uint64_t* o_free = bars + 18;     // [2] per O buffer (4 softmax warps arrive)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z;
+  const int h0 = blockIdx.y * heads_per_cta;
+  const int nh = min(heads_per_cta, H - h0);
+  const int q0 = blockIdx.x * kQ;
+  const int len = min(lengths[b], L);
+  const int inner = H * kDh;
+  const size_t row0 = static_cast<size_t>(b) * L;
+  const int n_kt = (len + kKeys - 1) / kKeys;
+  const int n_steps = nh * n_kt;
+
+  if (q0 >= len || nh <= 0) {
+    // every query row of this CTA is padding: zero output rows, no MMA work
+    for (int i = threadIdx.x; i < kQ * nh * (kDh / 8); i += blockDim.x) {
+      const int r = i / (nh * 8), rest = i % (nh * 8), hh = rest >> 3, c = rest & 7;
+      if (q0 + r < L)
+        *reinterpret_cast<uint4*>(out + (row0 + q0 + r) * inner + (h0 + hh) * kDh + c * 8) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < kKVStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tmQKV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  for (int i = threadIdx.x; i < nh * 2 * bt.half; i += blockDim.x) {
+    const int hh = i / (2 * bt.half), bk = i % (2 * bt.half);
+    sTab[hh * 64 + bk] = bias_tab[bk * H + h0 + hh] * 1.4426950408889634f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      for (int t = 0; t < n_steps && ok; ++t) {
+        const int hh = t / n_kt, j = t % n_kt, h = h0 + hh;
+        if (j == 0) {
+          // Q of head hh (single buffer: the last S of head hh - 1 must be done)
+          if (!(ok = mbar_wait(q_empty, (hh & 1) ^ 1, status))) break;
+          mbar_arrive_expect_tx(q_full, kQBytes);
+          tma_load_2d(sQ, &tmQKV, q_full, h * kDh, static_cast<int>(row0) + q0);  // box: 64 rows
+          tma_load_2d(sQ + kQBytes / 2, &tmQKV, q_full, h * kDh, static_cast<int>(row0) + q0 + 64);
+        }
+        const int s = t % kKVStages;
+        const uint32_t par = ((t / kKVStages) & 1) ^ 1;
+        if (!(ok = mbar_wait(&k_empty[s], par, status))) break;
+        mbar_arrive_expect_tx(&k_full[s], kKVBytes);
+        tma_load_2d(sK + s * kKVBytes, &tmQKV, &k_full[s], inner + h * kDh, static_cast<int>(row0) + j * kKeys);
+        if (!(ok = mbar_wait(&v_empty[s], par, status))) break;
+        mbar_arrive_expect_tx(&v_full[s], kKVBytes);
+        tma_load_2d(sV + s * kKVBytes, &tmQKV, &v_full[s], 2 * inner + h * kDh, static_cast<int>(row0) + j * kKeys);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16_f32(kQ, kKeys);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(kQ, kDh) | (1u << 16);  // B (V) MN-major
+      bool ok = true;
+      // S(t) = Q_h K_j^T into S buffer t % 2 (needs its Q and K/V stage)
+      auto issue_s = [&](int t) -> bool {
+        const int hh = t / n_kt, j = t % n_kt, s = t % kKVStages;
+        if (j == 0 && !mbar_wait(q_full, hh & 1, status)) return false;
+        if (!mbar_wait(&k_full[s], (t / kKVStages) & 1, status)) return false;
+        tc_fence_after();
+        const uint64_t qa = sw128_kmajor_desc(smem_u32(sQ));
+        const uint64_t bk = sw128_kmajor_desc(smem_u32(sK + s * kKVBytes));
+#pragma unroll
+        for (int k = 0; k < kDh / 16; ++k)
+          tc_mma_f16(tmem + kColS + 64 * (t & 1), qa + 2 * k, bk + 2 * k, idesc_qk, k > 0);
+        tc_commit(&s_full[t & 1]);
+        tc_commit(&k_empty[s]);
+        if (j == n_kt - 1) tc_commit(q_empty);  // last S of this head read its Q
+        return true;
+      };
+      for (int t = 0; t < 2 && t < n_steps && ok; ++t) ok = issue_s(t);
+      for (int t = 0; t < n_steps && ok; ++t) {
+        const int hh = t / n_kt, j = t % n_kt, s = t % kKVStages;
+        if (j == 0 && hh >= 2) {
+          // O buffer hh % 2 must be drained by the epilogue of head hh - 2
+          if (!(ok = mbar_wait(&o_free[hh & 1], ((hh >> 1) - 1) & 1, status))) break;
+        }
+        if (!(ok = mbar_wait(p_full, t & 1, status))) break;
+        if (!(ok = mbar_wait(&v_full[s], (t / kKVStages) & 1, status))) break;
+        tc_fence_after();
+        const uint64_t v = sw128_mnmajor_desc(smem_u32(sV + s * kKVBytes));
+        const uint64_t pa = sw128_kmajor_desc(smem_u32(sP + (t & 1) * kPBytes));
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k)
+          tc_mma_f16(tmem + kColO + 64 * (hh & 1), pa + 2 * k, v + 128 * k, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        tc_commit(o_done);
+        tc_commit(&v_empty[s]);
+        if (t + 2 < n_steps) ok = issue_s(t + 2);  // S buffer t % 2 is free again
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int st = threadIdx.x - 64;  // 0..127
+    const int qd = warp & 3;          // TMEM lane quarter
+    const int r = qd * 32 + lane;     // query row within the tile
+    const int qi = q0 + r;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    // Every step passes the named barrier, even after a failed wait, so a
+    // timed-out warp can never strand the other softmax warps there.
+    for (int t = 0; t < n_steps; ++t) {
+      const int hh = t / n_kt, j = t % n_kt;
+      const int k0 = j * kKeys;
+      if (j == 0) {
+        m_run = -INFINITY;
+        l_run = 0.f;
+      }
+      // bias window of this step: win[e] for key - query = k0 - q0 - (kQ - 1) + e
+      float* win = sWin + (t & 1) * (kWin + 1);
+      const float* tab = sTab + hh * 64;
+      for (int e = st; e < kWin; e += 128) win[e] = tab[rel_bucket_tc(bt, k0 - q0 - (kQ - 1) + e)];
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const float* brow = win + (kQ - 1) - r;  // bias of key k0 + c at brow[c]
+      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[t & 1], (t >> 1) & 1, status));
+      if (ok) {
+        // S(t) was issued after P(t-2) V(t-2): P buffer t % 2 is free again
+        tc_fence_after();
+        float v[kKeys];
+        tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1), &v[0]);
+        tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1) + 32, &v[32]);
+        tmem_wait_ld();
+        float tmax = -INFINITY;
+        if (k0 + kKeys <= len) {
+#pragma unroll
+          for (int i = 0; i < kKeys; ++i) {
+            v[i] = fmaf(v[i], 1.4426950408889634f, brow[i]);
+            tmax = fmaxf(tmax, v[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < kKeys; ++i) {
+            v[i] = (k0 + i < len) ? fmaf(v[i], 1.4426950408889634f, brow[i]) : -INFINITY;
+            tmax = fmaxf(tmax, v[i]);
+          }
+        }
+        // Lazy rescale: keep the running max unless this tile raises it by
+        // more than 8 (log2 units), so P stays <= 2^8 and O is rescaled
+        // rarely; the final division by the matching sum makes it exact.
+        const float m_new = (tmax > m_run + 8.0f) ? tmax : m_run;
+        const float corr = ex2(m_run - m_new);  // 1 when kept, 0 on the head's first tile
+        float psum = 0.f;
+        uint8_t* pbuf = sP + (t & 1) * kPBytes;
+#pragma unroll
+        for (int c = 0; c < kKeys; c += 8) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            const float p0 = ex2(v[c + i] - m_new), p1 = ex2(v[c + i + 1] - m_new);
+            psum += p0 + p1;
+            pk[i >> 1] = pack_f16x2(p0, p1);
+          }
+          *reinterpret_cast<uint4*>(pbuf + sw128_offset(r, c >> 3)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+        l_run = l_run * corr + psum;
+        m_run = m_new;
+        if (j > 0 && __any_sync(0xFFFFFFFFu, corr != 1.0f)) {
+          // O holds P(t-1) V(t-1) of this head once o_done says so; rescale it
+          // to the new max (rare with the lazy rule above)
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(o_done, (t - 1) & 1, status));
+          if (ok) {
+            tc_fence_after();
+            const uint32_t ocol = trow + kColO + 64 * (hh & 1);
+#pragma unroll 1
+            for (int c = 0; c < kDh; c += 32) {
+              float o[32];
+              tmem_ld_32x32b_x32(ocol + c, o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] *= corr;
+              tmem_st_32x32b_x32(ocol + c, o);
+            }
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (j == n_kt - 1) {
+        // epilogue of head h: O / l -> f16, then release the O buffer
+        if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(o_done, t & 1, status));
+        if (ok) {
+          tc_fence_after();
+          const float inv = 1.0f / l_run;
+          const uint32_t ocol = trow + kColO + 64 * (hh & 1);
+#pragma unroll 1
+          for (int c = 0; c < kDh; c += 32) {
+            float o[32];
+            tmem_ld_32x32b_x32(ocol + c, o);
+            if (qi < L) {
+              __half* dst = out + (row0 + qi) * inner + (h0 + hh) * kDh + c;
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                uint4 w;
+                w.x = pack_f16x2_sat(o[i] * inv, o[i + 1] * inv);
+                w.y = pack_f16x2_sat(o[i + 2] * inv, o[i + 3] * inv);
+                w.z = pack_f16x2_sat(o[i + 4] * inv, o[i + 5] * inv);
+                w.w = pack_f16x2_sat(o[i + 6] * inv, o[i + 7] * inv);
+                *reinterpret_cast<uint4*>(dst + i) = w;
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[hh & 1]);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const int32_t* lengths, int B, int L, int H,
+                                const float* bias_tab, const BucketThresholds& bt, uint32_t* status,
+                                cudaStream_t st) {
+  if (B <= 0 || L <= 0) return cudaSuccess;
+  if (L > kMaxL || 2 * bt.half > 64) return cudaErrorInvalidValue;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  // Heads per CTA: a CTA walks (head, key tile) steps as one pipeline, so
+  // short sequences take several heads per CTA to amortise its set-up, long
+  // ones one head (more, shorter CTAs balance the waves better); measured on
+  // B200 at L = 32, 182 and 512.
+  const int q_tiles = (L + kQ - 1) / kQ;
+  int hpc = std::min(std::min(H, kMaxHeads), std::max(1, (256 + L - 1) / L));
+  // ... but never fewer than about two CTAs per SM while heads can be split
+  while (hpc > 1 && static_cast<int64_t>(q_tiles) * B * ((H + hpc - 1) / hpc) < 2 * 148) --hpc;
+  const int groups = (H + hpc - 1) / hpc;
+  hpc = (H + groups - 1) / groups;  // balance the groups
+  dim3 grid(q_tiles, groups, B);
+  attention_tc_kernel<<<grid, kThreads, kSmem, st>>>(tm_qkv, out, lengths, L, H, hpc, bias_tab, bt, status);
+  return cudaGetLastError();
+}
+
+}  // namespace wc

@@ -63,13 +63,13 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// f16 activation matrix [rows][K], box 64 x 128, 128-byte swizzle.
-bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K) {
+// f16 activation matrix [rows][K], box 64 x box_rows, 128-byte swizzle.
+bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K, uint32_t box_rows = 128) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {K, rows};
   cuuint64_t strides[1] = {K * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, box_rows};
   cuuint32_t es[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -275,6 +275,8 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
   const T5Config& c = h->cfg;
   const int D = c.d_model, F = c.d_ff, I = h->inner, H = c.num_heads;
   const int M = B * L;
+  CUtensorMap tm_qkv;
+  if (!make_act_map(&tm_qkv, h->qkv, M, 3 * I, 64)) return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for qkv");
   cudaError_t e;
   if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, h->x, h->xn, st)) !=
       cudaSuccess)
@@ -284,7 +286,8 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
     LayerW& w = h->layers[l];
     if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, h->qkv, 3 * I, st, h->xn, w.qkv, w.qkv)))
       return rc;
-    if ((e = attention_launch(h->qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
+    if ((e = attention_tc_launch(tm_qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) !=
+        cudaSuccess)
       return cuda_fail(h, e, "attention launch");
     if ((rc = layer_gemm(h, kEpiF32, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, h->qkv, D, st, h->att, w.o, w.o))) return rc;
     if ((e = rmsnorm_launch(h->x, reinterpret_cast<const float*>(h->qkv), w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
@@ -753,8 +756,12 @@ extern "C" int wc_attention(const void* d_qkv, int B, int L, int H, const int32_
       num_buckets < 2 || num_buckets > 64 || max_distance < 1)
     return WC_E_INVALID_ARG;
   const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
-  return attention_launch(static_cast<const __half*>(d_qkv), static_cast<__half*>(d_out), d_lengths,
-                          B, L, H, d_bias_table, bt, static_cast<cudaStream_t>(stream)) == cudaSuccess
+  CUtensorMap tm;
+  if (!make_act_map(&tm, d_qkv, static_cast<uint64_t>(B) * L, 3 * H * 64, 64)) return WC_E_CUDA;
+  uint32_t* status = kernel_status_word();
+  if (!status) return WC_E_CUDA;
+  return attention_tc_launch(tm, static_cast<__half*>(d_out), d_lengths, B, L, H, d_bias_table, bt, status,
+                             static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? WC_OK
              : WC_E_CUDA;
 }
@@ -827,6 +834,8 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   const T5Config& c = h->cfg;
   const int D = c.d_model, F = c.d_ff, I = h->inner, H = c.num_heads;
   const int M = B * L;
+  CUtensorMap tm_qkv;
+  if (!make_act_map(&tm_qkv, qkv, M, 3 * I, 64)) return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for qkv");
   cudaError_t e;
   if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, x, xn, st)) !=
       cudaSuccess)
@@ -835,7 +844,7 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
     if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
-    if ((e = attention_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)) != cudaSuccess)
+    if ((e = attention_tc_launch(tm_qkv, att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
     if ((rc = layer_gemm(h, kEpiF32, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, qkv, D, st, att, w.o, w.o))) return rc;
     if ((e = rmsnorm_launch(x, reinterpret_cast<const float*>(qkv), w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
