@@ -18,12 +18,12 @@
 // the wi_1 rows of the same 128 features, so accumulator columns [0, 128) are
 // gate and [128, 256) are up for every row.
 //
-// Warp roles (576 threads per CTA):
+// Warp roles (448 threads per CTA):
 //   warp 0      TMA producer (X stages; raw Q4_K stages)
 //   warp 1      TMEM allocation; MMA issue (even CTA, one thread)
 //   warps 2-9   dequant: raw Q4_K -> f16 K-major 128-B-swizzled B stages
-//   warps 10-17 epilogue: tcgen05.ld -> registers -> global (two warps per
-//               TMEM lane quarter, one per column half)
+//   warps 10-13 epilogue: tcgen05.ld -> registers -> swizzled smem staging ->
+//               TMA tensor store (kEpiResid: read-modify-write of global)
 // Cross-CTA signalling: X loads of both CTAs complete on the even CTA's
 // barrier; dequant and epilogue warps arrive on the even CTA's barriers
 // through shared::cluster addresses; MMA completion is committed to both
@@ -42,7 +42,7 @@ constexpr int kBM = 256;          // rows per cluster tile (128 per CTA)
 constexpr int kBN = 256;          // columns per tile (128 weight rows per CTA)
 constexpr int kBK = 64;
 constexpr int kHalfN = kBN / 2;   // weight rows dequantised by one CTA
-constexpr int kSA = 6;            // X ring depth
+constexpr int kSA = 4;            // X ring depth
 constexpr int kSW = 3;            // raw Q4_K ring depth (super-blocks)
 constexpr int kSB = 4;            // dequantised B ring depth
 constexpr int kABytes = 128 * kBK * 2;
@@ -51,13 +51,11 @@ constexpr int kBBytes = kHalfN * kBK * 2;
 constexpr int kOffA = 0;
 constexpr int kOffW = kOffA + kSA * kABytes;
 constexpr int kOffB = kOffW + kSW * kWBytes;
-constexpr int kOffBar = kOffB + kSB * kBBytes;
+constexpr int kOutBytes = 32 * 128;  // one staged 32-row x 128-byte output chunk
+constexpr int kOffOut = kOffB + kSB * kBBytes;  // [epilogue warp][2] staged chunks
+constexpr int kOffBar = kOffOut + 4 * 2 * kOutBytes;
 constexpr int kSmem = 1024 + kOffBar + 512;
-#ifndef WC_GEMM2_EPI_WARPS
-#define WC_GEMM2_EPI_WARPS 4
-#endif
-constexpr int kEpiWarps = WC_GEMM2_EPI_WARPS;  // multiple of 4
-constexpr int kEpiSplit = kEpiWarps / 4;       // column parts per TMEM lane quarter
+constexpr int kEpiWarps = 4;  // one per TMEM lane quarter
 constexpr int kThreads = 64 + 256 + 32 * kEpiWarps;
 constexpr int kDequantWarps = 8;
 constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
@@ -194,7 +192,8 @@ __device__ __forceinline__ uint4 dequant8_f16(uint32_t x0, uint32_t x1, uint64_t
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_q4k_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
-                     const __grid_constant__ CUtensorMap tmW1, GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmOut,
+                     GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem + kOffA;
@@ -357,9 +356,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = (warp - 10) >> 2;  // column part of the tile
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
+    uint8_t* sOutW = smem + kOffOut + (warp - 10) * 2 * kOutBytes;
+    uint32_t ostage = 0;
     const uint32_t acc_empty_leader0 = map_to_rank(&acc_empty[0], 0);
     uint32_t it = 0;
     for (int tile = cid; tile < n_total; tile += ncl, ++it) {
@@ -370,60 +370,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + row;
       const int nt = tile % n_tiles;
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
-      if (EPI == kEpiGeGLU) {
+      if (EPI == kEpiResid) {
+        // residual read-modify-write (kernel-level entry point only)
 #pragma unroll 1
-        for (int c = half * (kHalfN / kEpiSplit); c < (half + 1) * (kHalfN / kEpiSplit); c += 32) {
-          float g[32], u[32];
-          tmem_ld_32x32b_x32(tb + c, g);
-          tmem_ld_32x32b_x32(tb + kHalfN + c, u);
+        for (int c = 0; c < kBN; c += 32) {
+          float v[32];
+          tmem_ld_32x32b_x32(tb + c, v);
           if (m < p.M) {
-            __half* out = reinterpret_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + nt * kHalfN + c;
+            float* out = reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + nt * kBN + c;
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 o;
-              o.x = pack_f16x2_sat(gelu_tanh_fast(g[i]) * u[i], gelu_tanh_fast(g[i + 1]) * u[i + 1]);
-              o.y = pack_f16x2_sat(gelu_tanh_fast(g[i + 2]) * u[i + 2], gelu_tanh_fast(g[i + 3]) * u[i + 3]);
-              o.z = pack_f16x2_sat(gelu_tanh_fast(g[i + 4]) * u[i + 4], gelu_tanh_fast(g[i + 5]) * u[i + 5]);
-              o.w = pack_f16x2_sat(gelu_tanh_fast(g[i + 6]) * u[i + 6], gelu_tanh_fast(g[i + 7]) * u[i + 7]);
-              *reinterpret_cast<uint4*>(out + i) = o;
+            for (int i = 0; i < 32; i += 4) {
+              float4 x = *reinterpret_cast<const float4*>(out + i);
+              x.x += v[i];
+              x.y += v[i + 1];
+              x.z += v[i + 2];
+              x.w += v[i + 3];
+              *reinterpret_cast<float4*>(out + i) = x;
             }
           }
         }
       } else {
+        // Each 128-byte-wide chunk of this warp's 32 rows is converted into
+        // a swizzled staging buffer and written by one TMA tensor store
+        // (rows past M are clipped by the tensor map), so global writes are
+        // whole lines instead of one 16-byte piece per row per instruction.
+        constexpr int kCW = EPI == kEpiF32 ? 32 : 64;         // output columns per chunk
+        constexpr int kOutCols = EPI == kEpiGeGLU ? kHalfN : kBN;
+        const int col_base = nt * kOutCols;
+        const int y0 = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + q * 32;
 #pragma unroll 1
-        for (int c = half * (kBN / kEpiSplit); c < (half + 1) * (kBN / kEpiSplit); c += 32) {
-          float v[32];
-          tmem_ld_32x32b_x32(tb + c, v);
-          if (m < p.M) {
-            const size_t off = static_cast<size_t>(m) * p.ldo + nt * kBN + c;
-            if (EPI == kEpiF16) {
-              __half* out = reinterpret_cast<__half*>(p.out) + off;
+        for (int c = 0; c < kOutCols; c += kCW, ++ostage) {
+          uint8_t* sbuf = sOutW + (ostage & 1) * kOutBytes;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+          uint8_t* srow = sbuf + lane * 128;
+          if (EPI == kEpiF32) {
+            float v[32];
+            tmem_ld_32x32b_x32(tb + c, v);
 #pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 o;
-                o.x = pack_f16x2_sat(v[i], v[i + 1]);
-                o.y = pack_f16x2_sat(v[i + 2], v[i + 3]);
-                o.z = pack_f16x2_sat(v[i + 4], v[i + 5]);
-                o.w = pack_f16x2_sat(v[i + 6], v[i + 7]);
-                *reinterpret_cast<uint4*>(out + i) = o;
+            for (int k = 0; k < 8; ++k)
+              *reinterpret_cast<float4*>(srow + ((k ^ (lane & 7)) << 4)) =
+                  make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          } else {
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {  // two 32-column halves of the 64-column chunk
+              float v[32];
+              tmem_ld_32x32b_x32(tb + c + 32 * hc, v);
+              if (EPI == kEpiGeGLU) {
+                float u[32];
+                tmem_ld_32x32b_x32(tb + kHalfN + c + 32 * hc, u);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_fast(v[i]) * u[i];
               }
-            } else if (EPI == kEpiF32) {
-              float* out = reinterpret_cast<float*>(p.out) + off;
 #pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-            } else {  // kEpiResid
-              float* out = reinterpret_cast<float*>(p.out) + off;
-#pragma unroll
-              for (int i = 0; i < 32; i += 4) {
-                float4 x = *reinterpret_cast<const float4*>(out + i);
-                x.x += v[i];
-                x.y += v[i + 1];
-                x.z += v[i + 2];
-                x.w += v[i + 3];
-                *reinterpret_cast<float4*>(out + i) = x;
+              for (int k = 0; k < 4; ++k) {
+                uint4 o;
+                o.x = pack_f16x2_sat(v[8 * k], v[8 * k + 1]);
+                o.y = pack_f16x2_sat(v[8 * k + 2], v[8 * k + 3]);
+                o.z = pack_f16x2_sat(v[8 * k + 4], v[8 * k + 5]);
+                o.w = pack_f16x2_sat(v[8 * k + 6], v[8 * k + 7]);
+                *reinterpret_cast<uint4*>(srow + (((4 * hc + k) ^ (lane & 7)) << 4)) = o;
               }
             }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            asm volatile(
+                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                    reinterpret_cast<uint64_t>(&tmOut)),
+                "r"(smem_u32(sbuf)), "r"(col_base + c), "r"(y0)
+                : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
         }
       }
@@ -431,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc_empty_leader0 + buf * 8);
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
 
   // ------------------------------------------------------------ teardown
@@ -444,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int EPI>
-cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const GemmParams& p,
-                   int num_sms, cudaStream_t st) {
+cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& out,
+                   const GemmParams& p, int num_sms, cudaStream_t st) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -469,7 +488,7 @@ cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMa
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm2_q4k_kernel<EPI>, a, w0, w1, p);
+  return cudaLaunchKernelEx(&cfg, gemm2_q4k_kernel<EPI>, a, w0, w1, out, p);
 }
 
 }  // namespace
@@ -480,12 +499,12 @@ bool gemm2_q4k_supports(int epi, int M, int N, int K) {
 }
 
 cudaError_t gemm2_q4k_launch(int epi, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
-                             const GemmParams& p, int num_sms, cudaStream_t st) {
+                             const CUtensorMap& out, const GemmParams& p, int num_sms, cudaStream_t st) {
   switch (epi) {
-    case kEpiF16: return launch<kEpiF16>(a, w0, w1, p, num_sms, st);
-    case kEpiGeGLU: return launch<kEpiGeGLU>(a, w0, w1, p, num_sms, st);
-    case kEpiResid: return launch<kEpiResid>(a, w0, w1, p, num_sms, st);
-    case kEpiF32: return launch<kEpiF32>(a, w0, w1, p, num_sms, st);
+    case kEpiF16: return launch<kEpiF16>(a, w0, w1, out, p, num_sms, st);
+    case kEpiGeGLU: return launch<kEpiGeGLU>(a, w0, w1, out, p, num_sms, st);
+    case kEpiResid: return launch<kEpiResid>(a, w0, w1, out, p, num_sms, st);
+    case kEpiF32: return launch<kEpiF32>(a, w0, w1, out, p, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
 }

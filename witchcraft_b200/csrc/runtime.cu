@@ -76,6 +76,21 @@ bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K, ui
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// GEMM output matrix [rows][cols] (f16 or f32) for TMA tensor stores: box of
+// 128 bytes x 32 rows, 128-byte swizzle.
+bool make_out_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols, bool f32) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const uint64_t esz = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * esz};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), 32};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims,
+             strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // raw Q4_K matrix [rows][K/256 * 144 bytes], box 144 x box_rows, no swizzle.
 bool make_q4k_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K, uint32_t box_rows) {
   EncodeTiledFn enc = get_encode_fn();
@@ -264,7 +279,10 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
     p.out = out;
     p.ldo = ldo;
     p.status = h->d_status;
-    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, p, device_sm_count(h->device), st);
+    CUtensorMap tm_out = a;
+    if (epi != kEpiResid && !make_out_map(&tm_out, out, M, ldo, epi == kEpiF32))
+      return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a GEMM output");
+    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, device_sm_count(h->device), st);
     return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
   }
   return gemm(h, epi, bn, a, w0, w1, M, N, K, out, ldo, st);
@@ -722,9 +740,11 @@ extern "C" int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const
     p.ldo = N;
     p.status = kernel_status_word();
     if (!p.status) return WC_E_CUDA;
+    CUtensorMap tout = ta;
+    if (epilogue != kEpiResid && !make_out_map(&tout, d_out, M, N, epilogue == kEpiF32)) return WC_E_CUDA;
     int dev = 0;
     cudaGetDevice(&dev);
-    return gemm2_q4k_launch(epilogue, ta, tw0, tw1, p, device_sm_count(dev), static_cast<cudaStream_t>(stream)) ==
+    return gemm2_q4k_launch(epilogue, ta, tw0, tw1, tout, p, device_sm_count(dev), static_cast<cudaStream_t>(stream)) ==
                    cudaSuccess
                ? WC_OK
                : WC_E_CUDA;
