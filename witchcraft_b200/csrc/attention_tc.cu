@@ -110,12 +110,14 @@ constexpr int kOffV = kOffK + kKVStages * kKVBytes;   // kKVStages stages
 constexpr int kOffP = kOffV + kKVStages * kKVBytes;   // 2 buffers
 constexpr int kOffWin = kOffP + 2 * kPBytes;  // f32 [2][kWin + 1]
 constexpr int kOffTab = kOffWin + 2 * (kWin + 1) * 4;  // f32 [kMaxHeads][64]
-constexpr int kOffBar = kOffTab + kMaxHeads * 64 * 4;
+constexpr int kMaxL = 2048;
+constexpr int kMaxTiles = kMaxL / kKeys;
+constexpr int kOffBkt = kOffTab + kMaxHeads * 64 * 4;  // u8 [key tile][kWin + 1] bucket indices
+constexpr int kOffBar = kOffBkt + ((kMaxTiles * (kWin + 1) + 127) / 128) * 128;
 constexpr int kSmem = 1024 + kOffBar + 256;
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128;  // S buffers at 0 / 64, O buffers at 128 / 192
-constexpr int kMaxL = 2048;
 
 __global__ void __launch_bounds__(kThreads)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __half* __restrict__ out,
@@ -129,6 +131,7 @@ __global__ void __launch_bounds__(kThreads)
   uint8_t* sP = smem + kOffP;
   float* sWin = reinterpret_cast<float*>(smem + kOffWin);
   float* sTab = reinterpret_cast<float*>(smem + kOffTab);  // [head in group][bucket] * log2(e)
+  uint8_t* sBkt = smem + kOffBkt;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars;          // [1]
   uint64_t* q_empty = bars + 1;     // [1]
@@ -184,6 +187,12 @@ __global__ void __launch_bounds__(kThreads)
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
+  }
+  // bucket of key - query = j * kKeys - q0 - (kQ - 1) + e for every key tile j
+  // of this CTA, computed once (the threshold loop is the expensive part)
+  for (int i = threadIdx.x; i < n_kt * (kWin + 1); i += blockDim.x) {
+    const int j = i / (kWin + 1), e = i - j * (kWin + 1);
+    sBkt[i] = static_cast<uint8_t>(rel_bucket_tc(bt, j * kKeys - q0 - (kQ - 1) + e));
   }
   for (int i = threadIdx.x; i < nh * 2 * bt.half; i += blockDim.x) {
     const int hh = i / (2 * bt.half), bk = i % (2 * bt.half);
@@ -280,7 +289,7 @@ __global__ void __launch_bounds__(kThreads)
       // bias window of this step: win[e] for key - query = k0 - q0 - (kQ - 1) + e
       float* win = sWin + (t & 1) * (kWin + 1);
       const float* tab = sTab + hh * 64;
-      for (int e = st; e < kWin; e += 128) win[e] = tab[rel_bucket_tc(bt, k0 - q0 - (kQ - 1) + e)];
+      for (int e = st; e < kWin; e += 128) win[e] = tab[sBkt[j * (kWin + 1) + e]];
       asm volatile("bar.sync 1, 128;" ::: "memory");
       const float* brow = win + (kQ - 1) - r;  // bias of key k0 + c at brow[c]
       if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[t & 1], (t >> 1) & 1, status));
@@ -291,26 +300,29 @@ __global__ void __launch_bounds__(kThreads)
         tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1), &v[0]);
         tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1) + 32, &v[32]);
         tmem_wait_ld();
-        float tmax = -INFINITY;
+        float mx[8] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY, -INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (k0 + kKeys <= len) {
 #pragma unroll
           for (int i = 0; i < kKeys; ++i) {
             v[i] = fmaf(v[i], 1.4426950408889634f, brow[i]);
-            tmax = fmaxf(tmax, v[i]);
+            mx[i & 7] = fmaxf(mx[i & 7], v[i]);  // 8 independent chains
           }
         } else {
 #pragma unroll
           for (int i = 0; i < kKeys; ++i) {
             v[i] = (k0 + i < len) ? fmaf(v[i], 1.4426950408889634f, brow[i]) : -INFINITY;
-            tmax = fmaxf(tmax, v[i]);
+            mx[i & 7] = fmaxf(mx[i & 7], v[i]);
           }
         }
+        const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
         // Lazy rescale: keep the running max unless this tile raises it by
         // more than 8 (log2 units), so P stays <= 2^8 and O is rescaled
         // rarely; the final division by the matching sum makes it exact.
         const float m_new = (tmax > m_run + 8.0f) ? tmax : m_run;
         const float corr = ex2(m_run - m_new);  // 1 when kept, 0 on the head's first tile
-        float psum = 0.f;
+        // p = 2^(t - max) -> f16 P row (K-major, 128-B swizzle), row sum in f32
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
         uint8_t* pbuf = sP + (t & 1) * kPBytes;
 #pragma unroll
         for (int c = 0; c < kKeys; c += 8) {
@@ -318,11 +330,12 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
           for (int i = 0; i < 8; i += 2) {
             const float p0 = ex2(v[c + i] - m_new), p1 = ex2(v[c + i + 1] - m_new);
-            psum += p0 + p1;
+            ps[i >> 1] += p0 + p1;
             pk[i >> 1] = pack_f16x2(p0, p1);
           }
           *reinterpret_cast<uint4*>(pbuf + sw128_offset(r, c >> 3)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
         l_run = l_run * corr + psum;
         m_run = m_new;
         if (j > 0 && __any_sync(0xFFFFFFFFu, corr != 1.0f)) {
