@@ -122,28 +122,31 @@ def _make_inputs(lengths, batch, rng):
     return ids, lens
 
 
-def cpu_reference_leg(model, lengths, target_s: float = 12.0, seed: int = 23):
-    """Times the CPU oracle (restatement of the reference's f32 CPU encoder)
-    on a bounded sample of config-4 documents with all host threads."""
-    from oracle import oracle as O
-    enc = O.OracleEncoder(model)
+def cpu_reference_leg(model, lengths, target_s: float = 12.0, seed: int = 23, enc=None):
+    """Times the reference's f32 CPU encoder algorithm, restated with torch's
+    MKL GEMMs (oracle/torch_ref.py), on a bounded sample of config-4
+    documents encoded one at a time as the reference's Embedder does, with
+    every host core (torchrun's OMP_NUM_THREADS=1 is overridden)."""
+    from oracle.torch_ref import TorchCPUEncoder
+    cores = os.cpu_count() or 1
+    enc = enc or TorchCPUEncoder(model, threads=cores)
     rng = np.random.default_rng(seed)
-    docs = rng.choice(len(lengths), 64, replace=False)
+    docs = rng.choice(len(lengths), 256, replace=False)
+    enc.encode_one(rng.integers(3, 32128, int(lengths[docs[0]])))  # warm the thread pool
     toks = 0
-    t0 = time.perf_counter()
     n_docs = 0
+    t0 = time.perf_counter()
     for d in docs:
         n = int(lengths[d])
-        ids = rng.integers(3, 32128, (1, n)).astype(np.uint32)
-        enc.encode(ids)
+        enc.encode_one(rng.integers(3, 32128, n))
         toks += n
         n_docs += 1
         if time.perf_counter() - t0 > target_s:
             break
     dt = time.perf_counter() - t0
-    return {"value": toks / dt, "unit": UNIT, "cores": O.num_threads(), "kind": "port",
-            "sample": f"{n_docs} config-4 documents ({toks} tokens) encoded one at a time (batch-1, as the "
-                      f"reference embeds), f32, oracle/oracle.c with OpenMP"}
+    return {"value": toks / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n_docs} config-4 documents ({toks} tokens) encoded one at a time (batch 1, as the "
+                      f"reference's Embedder does), f32, oracle/torch_ref.py (torch CPU, MKL GEMMs)"}
 
 
 def run_reference(args):
@@ -154,10 +157,12 @@ def run_reference(args):
     from witchcraft_b200.synth import make_synthetic_model
     model = make_synthetic_model(seed=0)
     lengths = shard.config4_lengths()
+    from oracle.torch_ref import TorchCPUEncoder
+    enc = TorchCPUEncoder(model, threads=os.cpu_count() or 1)
     vals = []
     leg = None
     for i in range(args.warmup + args.steps):
-        leg = cpu_reference_leg(model, lengths, target_s=args.ref_seconds, seed=100 + i)
+        leg = cpu_reference_leg(model, lengths, target_s=args.ref_seconds, seed=100 + i, enc=enc)
         if i >= args.warmup:
             vals.append(leg["value"])
     v = float(np.mean(vals))

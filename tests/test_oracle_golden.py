@@ -61,3 +61,12 @@ def test_padded_batch_equals_single_rows(tiny_model):
         single = enc.encode(ids[b:b + 1, :lens[b]])
         np.testing.assert_array_equal(batch[b, :lens[b]], single[0])
         assert np.all(batch[b, lens[b]:] == 0)
+
+
+def test_torch_cpu_restatement_matches_oracle(tiny_model):
+    """The torch-CPU f32 encoder bench.py times equals the C oracle."""
+    from oracle.torch_ref import TorchCPUEncoder
+    ids = np.random.default_rng(5).integers(3, 512, 37).astype(np.uint32)
+    got = TorchCPUEncoder(tiny_model, threads=2).encode_one(ids)
+    ref = O.OracleEncoder(tiny_model).encode(ids[None])[0]
+    np.testing.assert_allclose(got, ref, atol=2e-4, rtol=1e-4)
