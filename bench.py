@@ -41,8 +41,8 @@ UNIT = "tokens/s"
 MAX_BATCH_TOKENS = 16384
 LAUNCHES_PER_FORWARD_PER_LAYER = 7   # qkv gemm, attention, o gemm, rmsnorm, wi gemm, wo gemm, rmsnorm
 # dram read+write bytes per launch of the dominant kernel from the committed ncu
-# capture (profiles/gemm_geglu_m16384.md); None until a capture exists.
-NCU_TRAFFIC_BYTES = None
+# capture at M = 16,384.
+NCU_TRAFFIC_BYTES = 41278464  # 26.98 MB read + 14.30 MB written, profiles/gemm2_geglu_m16384.md
 
 
 def _peaks():
@@ -372,7 +372,7 @@ def kernel_measurements(enc, args, peak, peak_src):
 
     t, fl = gemm_case(16384, 768, 2048, 1, w0, w1)
     achieved = fl / t / 1e12
-    roof = {"bound": "tensor", "kernel": "gemm_q4k_kernel<256,kEpiGeGLU> (wi_0|wi_1 + gated GELU), M=16384 K=768 N=2x2048",
+    roof = {"bound": "tensor", "kernel": "gemm2_q4k_kernel<kEpiGeGLU> (wi_0|wi_1 + gated GELU, 2-SM), M=16384 K=768 N=2x2048",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_source": f"{peak_src} dense bf16/f16 burst", "traffic": NCU_TRAFFIC_BYTES,
             "avg_launch_us": t * 1e6, "algorithmic_flop_per_launch": fl}
