@@ -6,11 +6,12 @@
 //   per layer l:
 //     gemm  kEpiF16   qkv = xn . [Wq|Wk|Wv]^T                (f16 [M][3*inner])
 //     attention        att = softmax(QK^T + bias, key mask) V (f16 [M][inner])
-//     gemm  kEpiF32    y = att . Wo^T   (f32, into the dead qkv buffer)
-//     rmsnorm          x += y; xn = RMSNorm_ff(x)
+//     gemm  kEpiResid  x += att . Wo^T  (M >= 512: TMA load-add-store epilogue)
+//       (or kEpiF32    y = att . Wo^T into the dead qkv buffer, for small M)
+//     rmsnorm          (x += y;) xn = RMSNorm_ff(x)
 //     gemm  kEpiGeGLU  h = gelu(xn . Wi0^T) * (xn . Wi1^T)    (f16 [M][d_ff])
-//     gemm  kEpiF32    y = h . Wwo^T
-//     rmsnorm          x += y; xn = RMSNorm_{next attn | final}(x)
+//     gemm  kEpiResid  x += h . Wwo^T   (or kEpiF32 + add in the RMSNorm)
+//     rmsnorm          xn = RMSNorm_{next attn | final}(x)
 //   gemm  kEpiProj     out = xn . Wlin^T, norms, out / norm   (f32 [M][128])
 // following T5Stack::forward / T5Block::forward / T5EncoderModel::forward
 // (src/quantized_t5.rs:654-670, 598-628, 698-701).  The residual stream x
@@ -279,8 +280,8 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
     p.out = out;
     p.ldo = ldo;
     p.status = h->d_status;
-    CUtensorMap tm_out = a;
-    if (epi != kEpiResid && !make_out_map(&tm_out, out, M, ldo, epi == kEpiF32))
+    CUtensorMap tm_out;
+    if (!make_out_map(&tm_out, out, M, ldo, epi == kEpiF32 || epi == kEpiResid))
       return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a GEMM output");
     cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, device_sm_count(h->device), st);
     return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
@@ -295,6 +296,13 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
   const int M = B * L;
   CUtensorMap tm_qkv;
   if (!make_act_map(&tm_qkv, h->qkv, M, 3 * I, 64)) return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for qkv");
+  // Residual adds: for large M the O / wo GEMM epilogue adds into x itself
+  // (TMA load-add-store) and the RMSNorm only normalises; otherwise the GEMM
+  // writes f32 into the dead qkv buffer and the RMSNorm adds it.
+  const bool fused_res = M >= kGemm2MinRows;
+  const int res_epi = fused_res ? kEpiResid : kEpiF32;
+  void* res_out = fused_res ? static_cast<void*>(h->x) : static_cast<void*>(h->qkv);
+  const float* res_delta = fused_res ? nullptr : reinterpret_cast<const float*>(h->qkv);
   cudaError_t e;
   if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, h->x, h->xn, st)) !=
       cudaSuccess)
@@ -307,13 +315,13 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
     if ((e = attention_tc_launch(tm_qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) !=
         cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, h->qkv, D, st, h->att, w.o, w.o))) return rc;
-    if ((e = rmsnorm_launch(h->x, reinterpret_cast<const float*>(h->qkv), w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
+    if ((rc = layer_gemm(h, res_epi, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, res_out, D, st, h->att, w.o, w.o))) return rc;
+    if ((e = rmsnorm_launch(h->x, res_delta, w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
     if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, h->hbuf, F, st, h->xn, w.wi0, w.wi1))) return rc;
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, h->qkv, D, st, h->hbuf, w.wo, w.wo))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, res_out, D, st, h->hbuf, w.wo, w.wo))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
-    if ((e = rmsnorm_launch(h->x, reinterpret_cast<const float*>(h->qkv), next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
+    if ((e = rmsnorm_launch(h->x, res_delta, next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
   }
   return gemm(h, kEpiProj, 128, h->tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
@@ -740,8 +748,8 @@ extern "C" int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const
     p.ldo = N;
     p.status = kernel_status_word();
     if (!p.status) return WC_E_CUDA;
-    CUtensorMap tout = ta;
-    if (epilogue != kEpiResid && !make_out_map(&tout, d_out, M, N, epilogue == kEpiF32)) return WC_E_CUDA;
+    CUtensorMap tout;
+    if (!make_out_map(&tout, d_out, M, N, epilogue == kEpiF32 || epilogue == kEpiResid)) return WC_E_CUDA;
     int dev = 0;
     cudaGetDevice(&dev);
     return gemm2_q4k_launch(epilogue, ta, tw0, tw1, tout, p, device_sm_count(dev), static_cast<cudaStream_t>(stream)) ==
@@ -856,6 +864,10 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   const int M = B * L;
   CUtensorMap tm_qkv;
   if (!make_act_map(&tm_qkv, qkv, M, 3 * I, 64)) return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for qkv");
+  const bool fused_res = M >= kGemm2MinRows;  // as in forward_device
+  const int res_epi = fused_res ? kEpiResid : kEpiF32;
+  void* res_out = fused_res ? static_cast<void*>(x) : static_cast<void*>(qkv);
+  const float* res_delta = fused_res ? nullptr : reinterpret_cast<const float*>(qkv);
   cudaError_t e;
   if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, x, xn, st)) !=
       cudaSuccess)
@@ -866,12 +878,12 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
     if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
     if ((e = attention_tc_launch(tm_qkv, att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, qkv, D, st, att, w.o, w.o))) return rc;
-    if ((e = rmsnorm_launch(x, reinterpret_cast<const float*>(qkv), w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
+    if ((e = rmsnorm_launch(x, res_delta, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
     if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
-    if ((rc = layer_gemm(h, kEpiF32, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, qkv, D, st, hbuf, w.wo, w.wo))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
-    if ((e = rmsnorm_launch(x, reinterpret_cast<const float*>(qkv), next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    if ((e = rmsnorm_launch(x, res_delta, next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
   }
   return gemm(h, kEpiProj, 128, tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
               lengths, L);
