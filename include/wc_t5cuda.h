@@ -140,6 +140,13 @@ int wc_attention(const void* d_qkv, int B, int L, int H, const int32_t* d_length
  * or WC_E_INVALID_ARG. */
 int wc_t5_relative_bucket(int query, int key, int num_buckets, int max_distance);
 
+/* Failure-detection self-test (no counterpart in the reference, which has no
+ * device code): launches one warp whose mbarrier wait can never complete,
+ * bounded by limit_ns (1e6 .. 1e10).  Returns WC_E_TIMEOUT when the kernel
+ * gave up, reported it through the device status word and the CUDA context
+ * stayed usable afterwards; WC_E_CUDA otherwise.  Blocks until done. */
+int wc_selftest_wait_timeout(uint64_t limit_ns);
+
 #ifdef __cplusplus
 }
 #endif

@@ -153,3 +153,11 @@ def test_attention_config3_against_torch():
         rows = slice(b * L, b * L + lengths[b])
         assert (out[rows] - ref[rows]).abs().max().item() < 2e-2, b
         assert torch.all(torch.isfinite(out[b * L:(b + 1) * L]))
+
+
+def test_in_kernel_wait_timeout_is_reported():
+    """A wait that can never finish gives up after its limit, the kernel
+    reports WC_E_TIMEOUT through the status word, and the context still works."""
+    assert lib().wc_selftest_wait_timeout(20_000_000) == -5
+    g = np.load(os.path.join(GOLDEN, "q4k_golden.npz"))
+    assert _same_bits(dequant_gpu(g["blocks"]).cpu().numpy(), g["values"])

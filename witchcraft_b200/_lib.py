@@ -38,6 +38,7 @@ _SIGNATURES = {
     "wc_gemm_q4k": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "wc_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "wc_t5_relative_bucket": (c_int, [c_int, c_int, c_int, c_int]),
+    "wc_selftest_wait_timeout": (c_int, [ctypes.c_uint64]),
 }
 
 

@@ -10,7 +10,7 @@ namespace wc {
 // The T5 bidirectional bucket function of |key - query| is monotone, so it is
 // carried to the device as thresholds: bucket_half(d) = #{v in [1, half) :
 // thr[v] <= d}, plus `half` when the key comes after the query.  The host
-// derives thr[] from the reference's own f32 formula (see t5_buckets.h), so no
+// derives thr[] from the reference's own f32 formula (t5_bucket_thresholds in t5_host.h), so no
 // device logarithm ever decides a bucket.
 struct BucketThresholds {
   int half;      // num_buckets / 2

@@ -59,16 +59,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait for the phase with the given parity.  Returns false (and sets
 // kStatusWaitTimeout in *status) if the limit passes first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                                uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 255u && global_timer_ns() - t0 > limit_ns) {
       if (status) atomicOr(status, kStatusWaitTimeout);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  return mbar_wait_limit(bar, parity, status, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------- TMA

@@ -123,7 +123,24 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
   }
 }
 
+// A wait on an mbarrier that nothing ever arrives on, bounded by limit_ns:
+// exercises the timeout path every pipelined kernel uses.
+__global__ void wait_timeout_selftest_kernel(uint32_t* status, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  mbar_wait_limit(&bar, 0, status, limit_ns);
+}
+
 }  // namespace
+
+cudaError_t wait_timeout_selftest_launch(uint32_t* status, uint64_t limit_ns, cudaStream_t st) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, st>>>(status, limit_ns);
+  return cudaGetLastError();
+}
 
 cudaError_t q4k_dequant_launch(const uint8_t* blocks, int64_t nblocks, float* out, cudaStream_t st) {
   if (nblocks <= 0) return cudaSuccess;

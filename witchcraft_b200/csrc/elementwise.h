@@ -20,4 +20,8 @@ cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, cons
 cudaError_t rmsnorm_launch(float* x, const float* delta, const float* w, __half* y, int M, int D, float eps,
                            cudaStream_t st);
 
+// One warp waits on an mbarrier nobody arrives on, for at most limit_ns; the
+// timeout sets kStatusWaitTimeout in *status.
+cudaError_t wait_timeout_selftest_launch(uint32_t* status, uint64_t limit_ns, cudaStream_t st);
+
 }  // namespace wc

@@ -926,3 +926,15 @@ extern "C" int wc_t5_forward_device_noalloc(wc_t5* h, const uint32_t* d_ids, con
   if ((e = cudaMemsetAsync(h->d_status, 0, 4, st)) != cudaSuccess) return cuda_fail(h, e, "status reset");
   return forward_on(h, x, xn, qkv, att, hb, tm_xn, tm_att, tm_h, d_ids, d_lengths, B, L, d_out, d_norms, d_outn, st);
 }
+
+extern "C" int wc_selftest_wait_timeout(uint64_t limit_ns) {
+  if (limit_ns < 1000000ull || limit_ns > 10000000000ull) return WC_E_INVALID_ARG;
+  uint32_t* status = kernel_status_word();
+  if (!status) return WC_E_CUDA;
+  uint32_t s = 0;
+  if (cudaMemset(status, 0, 4) != cudaSuccess ||
+      wait_timeout_selftest_launch(status, limit_ns, nullptr) != cudaSuccess ||
+      cudaMemcpy(&s, status, 4, cudaMemcpyDeviceToHost) != cudaSuccess || cudaMemset(status, 0, 4) != cudaSuccess)
+    return WC_E_CUDA;  // the context did not stay usable
+  return (s & kStatusWaitTimeout) ? WC_E_TIMEOUT : WC_E_CUDA;
+}
