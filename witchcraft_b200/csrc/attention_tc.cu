@@ -145,6 +145,8 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* o_free = bars + 18;     // [2] per O buffer (4 softmax warps arrive)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
+  pdl_wait();  // before lengths and any activation (see pdl_wait)
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z;
   const int h0 = blockIdx.y * heads_per_cta;
@@ -428,8 +430,8 @@ cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const in
   const int groups = (H + hpc - 1) / hpc;
   hpc = (H + groups - 1) / groups;  // balance the groups
   dim3 grid(q_tiles, groups, B);
-  attention_tc_kernel<<<grid, kThreads, kSmem, st>>>(tm_qkv, out, lengths, L, H, hpc, bias_tab, bt, status);
-  return cudaGetLastError();
+  return launch_pdl(attention_tc_kernel, grid, dim3(kThreads), kSmem, st, nullptr, 0, tm_qkv, out, lengths, L, H, hpc,
+                    bias_tab, bt, status);
 }
 
 }  // namespace wc

@@ -8,7 +8,39 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <stdlib.h>
+
+#include <utility>
+
 namespace wc {
+
+// Launches kernel on `st` with programmatic stream serialisation (see
+// pdl_wait); extra launch attributes (e.g. a cluster shape) may be appended.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              const cudaLaunchAttribute* extra, int n_extra, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[4];
+  int n = 0;
+  // WC_DISABLE_PDL=1 turns the overlap off (griddepcontrol.* are then no-ops).
+  static const bool pdl_on = [] {
+    const char* e = getenv("WC_DISABLE_PDL");
+    return !(e && e[0] == '1');
+  }();
+  if (pdl_on) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  for (int i = 0; i < n_extra && n < 4; ++i) attrs[n++] = extra[i];
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Status bits a kernel ORs into the per-handle device status word instead of
 // trapping.  The host reads the word after each forward and turns a non-zero
@@ -74,6 +106,16 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
   return mbar_wait_limit(bar, parity, status, kWaitLimitNs);
 }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the forward is launched with programmatic stream
+// serialisation: it lets the next kernel start (pdl_launch_next) right away,
+// does only work that touches no activation (barrier init, TMEM allocation,
+// descriptor prefetch) and then waits (pdl_wait) for the previous kernel to
+// complete and flush before it reads or writes any activation buffer.  So the
+// launch latency and prologue of each kernel overlap its predecessor's tail.
+__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -39,6 +39,8 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
                                      const int32_t* __restrict__ lengths, int L, int M, int D,
                                      const float* __restrict__ w, float eps, float* __restrict__ x,
                                      __half* __restrict__ xn) {
+  pdl_wait();
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -84,6 +86,8 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
 // (written back), then the norm of the updated row.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                __half* __restrict__ y, int M, int D, float eps) {
+  pdl_wait();
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -154,16 +158,15 @@ cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, cons
                                  int D, const float* w, float eps, float* x, __half* xn, cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 256 != 0 || D > kMaxD) return cudaErrorInvalidValue;
-  embed_rmsnorm_kernel<<<(M + 7) / 8, 256, 0, st>>>(table, ids, lengths, L, M, D, w, eps, x, xn);
-  return cudaGetLastError();
+  return launch_pdl(embed_rmsnorm_kernel, dim3((M + 7) / 8), dim3(256), 0, st, nullptr, 0, table, ids, lengths, L, M, D,
+                    w, eps, x, xn);
 }
 
 cudaError_t rmsnorm_launch(float* x, const float* delta, const float* w, __half* y, int M, int D, float eps,
                            cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 128 != 0 || D > kMaxD) return cudaErrorInvalidValue;
-  rmsnorm_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, delta, w, y, M, D, eps);
-  return cudaGetLastError();
+  return launch_pdl(rmsnorm_kernel, dim3((M + 7) / 8), dim3(256), 0, st, nullptr, 0, x, delta, w, y, M, D, eps);
 }
 
 }  // namespace wc

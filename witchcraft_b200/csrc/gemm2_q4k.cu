@@ -254,6 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // every role touches activations only after this
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -511,19 +513,12 @@ cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMa
   }
   const int tiles = ((p.M + kBM - 1) / kBM) * (p.N / kBN);
   const int clusters = std::max(1, std::min(tiles, num_sms / 2));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmem;
-  cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm2_q4k_kernel<EPI>, a, w0, w1, out, p);
+  return launch_pdl(gemm2_q4k_kernel<EPI>, dim3(2 * clusters), dim3(kThreads), kSmem, st, attr, 1, a, w0, w1, out, p);
 }
 
 }  // namespace

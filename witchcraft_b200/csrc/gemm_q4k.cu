@@ -105,6 +105,8 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_acc = *tmem_slot;
+  pdl_wait();  // every role touches activations only after this
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -339,8 +341,7 @@ static cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& w0, const
   }
   const int n_tiles = p.N / BN;
   dim3 grid(n_tiles, (p.M + C::BM - 1) / C::BM);
-  gemm_q4k_kernel<BN, EPI><<<grid, C::THREADS, C::SMEM, st>>>(a, w0, w1, p);
-  return cudaGetLastError();
+  return launch_pdl(gemm_q4k_kernel<BN, EPI>, grid, dim3(C::THREADS), C::SMEM, st, nullptr, 0, a, w0, w1, p);
 }
 
 int gemm_q4k_bn_for(int epi, int N) {

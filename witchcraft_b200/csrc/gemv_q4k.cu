@@ -73,10 +73,8 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q4k_kernel(const __half* __r
   // super-block of this warp's rows), then waited for once.
   const int kb_per_warp = (kblocks + kWarps - 1) / kWarps;
   uint8_t* myW = sW + warp * kb_per_warp * NMAT * kRows * 144;
-  for (int i = tid; i < TOK * (K / 8); i += blockDim.x) {
-    const int r = i / (K / 8), c = i % (K / 8);
-    cp_async16(sX + r * xstride + c * 16, X + static_cast<size_t>(r < M ? r : 0) * K + c * 8, r < M);
-  }
+  // the raw weights are constant: request them before waiting for the
+  // previous kernel, the activations after
   for (int s = 0; s < kb_per_warp; ++s) {
     const int kb = warp + s * kWarps;
     if (kb >= kblocks) break;
@@ -85,6 +83,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q4k_kernel(const __half* __r
       const uint8_t* src = (rr < kRows ? W0 : W1) + (row0 + (rr % kRows)) * wrow_bytes + kb * 144 + c * 16;
       cp_async16(myW + (s * NMAT * kRows + rr) * 144 + c * 16, src, true);
     }
+  }
+  pdl_wait();
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
+  for (int i = tid; i < TOK * (K / 8); i += blockDim.x) {
+    const int r = i / (K / 8), c = i % (K / 8);
+    cp_async16(sX + r * xstride + c * 16, X + static_cast<size_t>(r < M ? r : 0) * K + c * 8, r < M);
   }
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
@@ -190,8 +194,8 @@ cudaError_t launch(const __half* X, int M, int K, const uint8_t* W0, const uint8
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  gemv_q4k_kernel<EPI, MT><<<N / kRows, kWarps * 32, smem, st>>>(X, M, K, W0, W1, out, ldo);
-  return cudaGetLastError();
+  return launch_pdl(gemv_q4k_kernel<EPI, MT>, dim3(N / kRows), dim3(kWarps * 32), smem, st, nullptr, 0, X, M, K, W0,
+                    W1, out, ldo);
 }
 
 template <int EPI>
