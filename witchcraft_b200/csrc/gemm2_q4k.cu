@@ -153,25 +153,6 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
       : "memory");
 }
 
-// Packed f32x2 arithmetic (one instruction for two lanes of f32 on sm_100).
-__device__ __forceinline__ uint64_t f2(float lo, float hi) {
-  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-// f16x2 of the two f32 lanes, round to nearest even.
-__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
-  return pack_f16x2(__uint_as_float(static_cast<uint32_t>(v)), __uint_as_float(static_cast<uint32_t>(v >> 32)));
-}
-
 // 8 weights from the nibbles in the bytes of x0, x1 (0..15 each):
 // d1*q - m1 exactly as the reference (see q4k.cuh), then f16.
 __device__ __forceinline__ uint4 dequant8_f16(uint32_t x0, uint32_t x1, uint64_t d1, uint64_t negm1) {
