@@ -4,10 +4,12 @@
 // scores without 1/sqrt(d) scaling, + position bias, softmax_last_dim, P.V,
 // transpose back to tokens.
 //
-// One CTA owns 128 queries of one sequence for a group of heads and walks the
-// flattened sequence of steps (head, 64-key tile) as one pipeline, so the
-// TMA loads and S MMAs of the next step -- also across a head boundary --
-// overlap the softmax of the current one:
+// Persistent: a grid of two CTAs per SM walks the items (sequence, 128-query
+// tile, head) with a static stride, and each CTA runs the flattened sequence
+// of its steps (item, 64-key tile) as one pipeline, so the TMA loads and S
+// MMAs of the next step -- also across an item boundary -- overlap the
+// softmax of the current one, and the set-up (barriers, TMEM, the bias
+// tables of all heads) is paid once per CTA:
 //   warp 0      TMA: the Q tile of each head (one shared-memory buffer),
 //               its K and V tiles (two 3-stage rings; a K stage is freed as
 //               soon as its S is done)
@@ -109,57 +111,136 @@ __device__ __forceinline__ int rel_bucket_tc(const int* thr, int half, int delta
 }
 
 
-#ifdef WC_ATTN_TRACE
-// Development instrumentation: per-CTA clock64 stamps of softmax thread 0.
-constexpr int kTraceCtas = 8192, kTraceSlots = 12;
-__device__ unsigned long long g_attn_trace[kTraceCtas][kTraceSlots];
-#define ATTN_TRACE(slot, val) \
-  if (threadIdx.x == 64 && trace_id < kTraceCtas) g_attn_trace[trace_id][slot] = (val)
-#define ATTN_TRACE_ADD(slot, val) tr_acc[slot] += (val)
-#else
-#define ATTN_TRACE(slot, val)
-#define ATTN_TRACE_ADD(slot, val)
-#endif
-
-constexpr int kQ = 128;       // queries per CTA
+constexpr int kQ = 128;       // queries per item
 constexpr int kKeys = 64;     // keys per tile
 constexpr int kDh = 64;
 constexpr int kQBytes = kQ * 128;      // 128 x 64 f16
 constexpr int kKVBytes = kKeys * 128;  // 64 x 64 f16
 constexpr int kWin = kQ + kKeys - 1;   // distinct key - query offsets of one tile pair
-constexpr int kMaxHeads = 16;          // heads of one CTA's group
+constexpr int kMaxHeads = 32;          // bias tables of all heads stay in shared memory
 constexpr int kKVStages = 3;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;                // kKVStages stages
 constexpr int kOffV = kOffK + kKVStages * kKVBytes;   // kKVStages stages
-// Bias window of one step in two copies, the second shifted by one entry, so
-// that every thread reads its biases as 8-byte aligned pairs.
-constexpr int kWinPad = kWin + 1;
-constexpr int kOffWin = kOffV + kKVStages * kKVBytes;  // f32 [2 steps][2 copies][kWinPad]
-constexpr int kOffTab = kOffWin + 2 * 2 * kWinPad * 4;  // f32 [kMaxHeads][64]
 constexpr int kMaxL = 2048;
+// Bias row of one item: bias[x] for key - query = x - q0 - (kQ - 1), built
+// once per item, in two copies, the second shifted by one entry, so that
+// every thread reads its biases as 8-byte aligned pairs; the copies are
+// 2256 = 16 (mod 32) words apart, so the neighbouring lanes that read the
+// same offsets from different copies fall in different banks.
+constexpr int kBiasPad = 2256;
+static_assert(kBiasPad >= kMaxL + kWin + 1 && kBiasPad % 32 == 16, "bias row copies");
+constexpr int kOffBias = kOffV + kKVStages * kKVBytes;  // f32 [2 copies][kBiasPad]
+constexpr int kOffTab = kOffBias + 2 * kBiasPad * 4;   // f32 [kMaxHeads][64]
 constexpr int kOffThr = kOffTab + kMaxHeads * 64 * 4;  // int [32]
-// u8 bucket of key - query = x - q0 - (kQ - 1) at index x
-constexpr int kOffBkt = kOffThr + 32 * 4;
-constexpr int kOffBar = kOffBkt + ((kMaxL + kWin + 127) / 128) * 128;
+constexpr int kMaxSortSeqs = 4096;  // larger batches keep their own sequence order
+constexpr int kOffOrder = kOffThr + 32 * 4;            // u16 [kMaxSortSeqs]
+constexpr int kOffHist = kOffOrder + kMaxSortSeqs * 2;                   // int [64]
+constexpr int kOffBar = kOffHist + 64 * 4;
 constexpr int kSmem = 1024 + kOffBar + 256;
 constexpr int kThreads = 192;
+constexpr int kCtasPerSm = 2;
 constexpr uint32_t kTmemCols = 256;
 // S (and P) buffers at 0 / 64, O at 128, Q buffers at 192 / 224
 constexpr uint32_t kColS = 0, kColO = 128, kColQ = 192;
 
+// One unit of work: the kQ queries from q0 of sequence b, head h.  Items
+// are numbered with the sequences in descending order of key tiles (the
+// order every CTA derives identically, see sort_sequences), then query tile,
+// then head; in round r a CTA takes item r * grid + its rank, its rank taken
+// from the other end in odd rounds, which balances the CTAs' work like
+// longest-first scheduling.  id >= n_items marks the end of a CTA's list.
+struct Item {
+  int id, round, b, q0, h, len, n_kt;
+};
+
+struct ItemList {
+  const int32_t* lengths;
+  const uint16_t* order;  // sorted sequence index, or null: identity
+  int n_items, q_tiles, H, L;
+
+  __device__ __forceinline__ int seq_len(int b) const { return max(0, min(lengths[b], L)); }
+  __device__ __forceinline__ Item decode(int round) const {
+    const int g = static_cast<int>(gridDim.x);
+    const int id = round * g + ((round & 1) ? g - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x));
+    Item it{id, round, 0, 0, 0, 0, 0};
+    if (id >= n_items) return it;
+    it.h = id % H;
+    const int rest = id / H;
+    it.q0 = (rest % q_tiles) * kQ;
+    const int pos = rest / q_tiles;
+    it.b = order ? order[pos] : pos;
+    it.len = seq_len(it.b);
+    it.n_kt = (it.len + kKeys - 1) / kKeys;
+    return it;
+  }
+  // This CTA's next item from round `round` on with at least one valid query.
+  __device__ __forceinline__ Item next_active(int round) const {
+    for (;; ++round) {
+      const Item it = decode(round);
+      if (it.id >= n_items || it.q0 < it.len) return it;
+    }
+  }
+};
+
+// Walks one CTA's steps: key tile j of its g-th active item.
+struct Cursor {
+  Item it;
+  int j, g;
+  __device__ __forceinline__ bool valid(const ItemList& il) const { return it.id < il.n_items; }
+  __device__ __forceinline__ void advance(const ItemList& il) {
+    if (++j == it.n_kt) {
+      it = il.next_active(it.round + 1);
+      j = 0;
+      ++g;
+    }
+  }
+};
+
+// One warp: order[pos] = the sequences by descending key-tile count, ties in
+// index order (a stable counting sort, so every CTA gets the same order).
+__device__ void sort_sequences(const ItemList& il, int B, uint16_t* order, int* hist, int lane) {
+  constexpr int kBins = kMaxL / kKeys + 1;
+  for (int i = lane; i < 64; i += 32) hist[i] = 0;
+  __syncwarp();
+  for (int b0 = 0; b0 < B; b0 += 32) {
+    const int b = b0 + lane;
+    const int key = b < B ? (il.seq_len(b) + kKeys - 1) / kKeys : -1;
+    const unsigned same = __match_any_sync(0xFFFFFFFFu, key);
+    if (key >= 0 && lane == __ffs(same) - 1) hist[key] += __popc(same);
+    __syncwarp();
+  }
+  if (lane == 0) {
+    int run = 0;  // exclusive prefix, largest key first
+    for (int k = kBins - 1; k >= 0; --k) {
+      const int c = hist[k];
+      hist[k] = run;
+      run += c;
+    }
+  }
+  __syncwarp();
+  for (int b0 = 0; b0 < B; b0 += 32) {
+    const int b = b0 + lane;
+    const int key = b < B ? (il.seq_len(b) + kKeys - 1) / kKeys : -1;
+    const unsigned same = __match_any_sync(0xFFFFFFFFu, key);
+    if (key >= 0) order[hist[key] + __popc(same & ((1u << lane) - 1u))] = static_cast<uint16_t>(b);
+    __syncwarp();
+    if (key >= 0 && lane == __ffs(same) - 1) hist[key] += __popc(same);
+    __syncwarp();
+  }
+}
+
 __global__ void __launch_bounds__(kThreads)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, __half* __restrict__ out,
-                        const int32_t* __restrict__ lengths, int L, int H, int heads_per_cta,
+                        const int32_t* __restrict__ lengths, int B, int L, int H,
                         const float* __restrict__ bias_tab, BucketThresholds bt, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + kOffQ;
   uint8_t* sK = smem + kOffK;
   uint8_t* sV = smem + kOffV;
-  float* sWin = reinterpret_cast<float*>(smem + kOffWin);
-  float* sTab = reinterpret_cast<float*>(smem + kOffTab);  // [head in group][bucket] * log2(e)
-  uint8_t* sBkt = smem + kOffBkt;
+  float* sBias = reinterpret_cast<float*>(smem + kOffBias);
+  float* sTab = reinterpret_cast<float*>(smem + kOffTab);  // [head][bucket] * log2(e)
   int* sThr = reinterpret_cast<int*>(smem + kOffThr);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars;          // [1]
@@ -169,46 +250,25 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* v_full = bars + 8;      // [kKVStages]
   uint64_t* v_empty = bars + 11;    // [kKVStages]  freed when P(t) V(t) is done
   uint64_t* s_full = bars + 14;     // [2] per S buffer
-  uint64_t* p_full = bars + 16;     // [1] (4 softmax warps arrive)
-  uint64_t* o_done = bars + 17;     // [1] one phase per step
-  uint64_t* q_tm = bars + 18;       // [2] per TMEM Q buffer (4 softmax warps arrive)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  // [2] by step parity (4 softmax warps arrive): the warps do not step in
+  // lockstep, one may arrive for step t + 1 before another for step t, but
+  // never for t + 2 (S(t + 2) is issued only after P(t))
+  uint64_t* p_full = bars + 16;
+  // [2] by step parity: P(t) V(t) done.  A softmax warp waits for P V of step
+  // t or t - 1 while only P V(t - 2) is known complete (its S(t) came after
+  // it); one barrier per step parity keeps that wait one phase deep, which a
+  // parity wait tells apart.
+  uint64_t* o_done = bars + 18;
+  uint64_t* q_tm = bars + 20;       // [2] per TMEM Q buffer (4 softmax warps arrive)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
 
-#ifdef WC_ATTN_TRACE
-  const int trace_id = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-  const unsigned long long tr0 = clock64();
-  unsigned long long tr_acc[kTraceSlots] = {};
-  if (threadIdx.x == 64 && trace_id < kTraceCtas)
-    for (int i = 0; i < kTraceSlots; ++i) g_attn_trace[trace_id][i] = 0;
-  ATTN_TRACE(0, tr0);
-  {
-    unsigned smid;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    ATTN_TRACE(8, smid);
-  }
-#endif
   pdl_wait();  // before lengths and any activation (see pdl_wait)
   pdl_launch_next();  // after the wait: at most one grid waits ahead
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z;
-  const int h0 = blockIdx.y * heads_per_cta;
-  const int nh = min(heads_per_cta, H - h0);
-  const int q0 = blockIdx.x * kQ;
-  const int len = min(lengths[b], L);
+  const int q_tiles = (L + kQ - 1) / kQ;
+  uint16_t* sOrder = reinterpret_cast<uint16_t*>(smem + kOffOrder);
+  const ItemList il{lengths, B <= kMaxSortSeqs ? sOrder : nullptr, B * q_tiles * H, q_tiles, H, L};
   const int inner = H * kDh;
-  const size_t row0 = static_cast<size_t>(b) * L;
-  const int n_kt = (len + kKeys - 1) / kKeys;
-  const int n_steps = nh * n_kt;
-
-  if (q0 >= len || nh <= 0) {
-    // every query row of this CTA is padding: zero output rows, no MMA work
-    for (int i = threadIdx.x; i < kQ * nh * (kDh / 8); i += blockDim.x) {
-      const int r = i / (nh * 8), rest = i % (nh * 8), hh = rest >> 3, c = rest & 7;
-      if (q0 + r < L)
-        *reinterpret_cast<uint4*>(out + (row0 + q0 + r) * inner + (h0 + hh) * kDh + c * 8) = make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -222,9 +282,9 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&q_tm[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
     mbar_fence_init();
     tma_prefetch_desc(&tmQKV);
   }
@@ -232,45 +292,48 @@ __global__ void __launch_bounds__(kThreads)
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
+  if (warp == 2 && il.order) sort_sequences(il, B, sOrder, reinterpret_cast<int*>(smem + kOffHist), lane);
   if (threadIdx.x < 32) sThr[threadIdx.x] = bt.thr[threadIdx.x];
-  __syncthreads();
-  // bucket of every key - query offset this CTA meets, once
-  for (int x = threadIdx.x; x < n_kt * kKeys + kWin; x += blockDim.x)
-    sBkt[x] = static_cast<uint8_t>(rel_bucket_tc(sThr, bt.half, x - q0 - (kQ - 1)));
-  for (int i = threadIdx.x; i < nh * 2 * bt.half; i += blockDim.x) {
-    const int hh = i / (2 * bt.half), bk = i % (2 * bt.half);
-    sTab[hh * 64 + bk] = bias_tab[bk * H + h0 + hh] * 1.4426950408889634f;
+  for (int i = threadIdx.x; i < H * 2 * bt.half; i += blockDim.x) {
+    const int h = i / (2 * bt.half), bk = i % (2 * bt.half);
+    sTab[h * 64 + bk] = bias_tab[bk * H + h] * 1.4426950408889634f;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  ATTN_TRACE(1, clock64());
-  ATTN_TRACE(7, n_steps);
+  const Cursor start{il.next_active(0), 0, 0};
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      // Q of head hq (single buffer, free once the previous head's Q is in TMEM)
-      auto load_q = [&](int hq) -> bool {
-        if (!mbar_wait(q_empty, (hq & 1) ^ 1, status)) return false;
+      // Q of the g-th active item (single buffer, free once the previous Q is in TMEM)
+      auto load_q = [&](const Item& it, int g) -> bool {
+        if (!mbar_wait(q_empty, (g & 1) ^ 1, status)) return false;
         mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_2d(sQ, &tmQKV, q_full, (h0 + hq) * kDh, static_cast<int>(row0) + q0);  // box: 64 rows
-        tma_load_2d(sQ + kQBytes / 2, &tmQKV, q_full, (h0 + hq) * kDh, static_cast<int>(row0) + q0 + 64);
+        const int row = it.b * L + it.q0;
+        tma_load_2d(sQ, &tmQKV, q_full, it.h * kDh, row);  // box: 64 rows
+        tma_load_2d(sQ + kQBytes / 2, &tmQKV, q_full, it.h * kDh, row + 64);
         return true;
       };
-      bool ok = load_q(0);
-      for (int t = 0; t < n_steps && ok; ++t) {
-        const int hh = t / n_kt, j = t % n_kt, h = h0 + hh;
-        if (j == 0 && hh + 1 < nh && !(ok = load_q(hh + 1))) break;
+      Cursor c = start;
+      bool ok = !c.valid(il) || load_q(c.it, 0);
+      for (int t = 0; c.valid(il) && ok; ++t) {
+        if (c.j == 0) {
+          // one item ahead
+          const Item nx = il.next_active(c.it.round + 1);
+          if (nx.id < il.n_items && !(ok = load_q(nx, c.g + 1))) break;
+        }
         const int s = t % kKVStages;
         const uint32_t par = ((t / kKVStages) & 1) ^ 1;
+        const int krow = c.it.b * L + c.j * kKeys;
         if (!(ok = mbar_wait(&k_empty[s], par, status))) break;
         mbar_arrive_expect_tx(&k_full[s], kKVBytes);
-        tma_load_2d(sK + s * kKVBytes, &tmQKV, &k_full[s], inner + h * kDh, static_cast<int>(row0) + j * kKeys);
+        tma_load_2d(sK + s * kKVBytes, &tmQKV, &k_full[s], inner + c.it.h * kDh, krow);
         if (!(ok = mbar_wait(&v_empty[s], par, status))) break;
         mbar_arrive_expect_tx(&v_full[s], kKVBytes);
-        tma_load_2d(sV + s * kKVBytes, &tmQKV, &v_full[s], 2 * inner + h * kDh, static_cast<int>(row0) + j * kKeys);
+        tma_load_2d(sV + s * kKVBytes, &tmQKV, &v_full[s], 2 * inner + c.it.h * kDh, krow);
+        c.advance(il);
       }
     }
   } else if (warp == 1) {
@@ -279,36 +342,42 @@ __global__ void __launch_bounds__(kThreads)
       constexpr uint32_t idesc_qk = idesc_f16_f32(kQ, kKeys);
       constexpr uint32_t idesc_pv = idesc_f16_f32(kQ, kDh) | (1u << 16);  // B (V) MN-major
       bool ok = true;
-      // S(t) = Q_h K_j^T into S buffer t % 2 (needs its Q and K/V stage)
-      auto issue_s = [&](int t) -> bool {
-        const int hh = t / n_kt, j = t % n_kt, s = t % kKVStages;
-        if (j == 0 && !mbar_wait(&q_tm[hh & 1], (hh >> 1) & 1, status)) return false;
-        if (!mbar_wait(&k_full[s], (t / kKVStages) & 1, status)) return false;
+      Cursor cs = start;  // next S to issue (two steps ahead of P V)
+      int ts = 0;
+      // S(ts) = Q K_j^T into S buffer ts % 2 (needs its Q and K stage)
+      auto issue_s = [&]() -> bool {
+        const int s = ts % kKVStages;
+        if (cs.j == 0 && !mbar_wait(&q_tm[cs.g & 1], (cs.g >> 1) & 1, status)) return false;
+        if (!mbar_wait(&k_full[s], (ts / kKVStages) & 1, status)) return false;
         tc_fence_after();
-        const uint32_t qa = tmem + kColQ + 32 * (hh & 1);
+        const uint32_t qa = tmem + kColQ + 32 * (cs.g & 1);
         const uint64_t bk = sw128_kmajor_desc(smem_u32(sK + s * kKVBytes));
 #pragma unroll
         for (int k = 0; k < kDh / 16; ++k)
-          tc_mma_f16_ts(tmem + kColS + 64 * (t & 1), qa + 8 * k, bk + 2 * k, idesc_qk, k > 0);
-        tc_commit(&s_full[t & 1]);
+          tc_mma_f16_ts(tmem + kColS + 64 * (ts & 1), qa + 8 * k, bk + 2 * k, idesc_qk, k > 0);
+        tc_commit(&s_full[ts & 1]);
         tc_commit(&k_empty[s]);
+        cs.advance(il);
+        ++ts;
         return true;
       };
-      for (int t = 0; t < 2 && t < n_steps && ok; ++t) ok = issue_s(t);
-      for (int t = 0; t < n_steps && ok; ++t) {
-        const int j = t % n_kt, s = t % kKVStages;
-        // P(t) also means the epilogue of the previous head has read O
-        if (!(ok = mbar_wait(p_full, t & 1, status))) break;
+      for (int k = 0; k < 2 && cs.valid(il) && ok; ++k) ok = issue_s();
+      Cursor cp = start;
+      for (int t = 0; cp.valid(il) && ok; ++t) {
+        const int s = t % kKVStages;
+        // P(t) also means the epilogue of the previous item has read O
+        if (!(ok = mbar_wait(&p_full[t & 1], (t >> 1) & 1, status))) break;
         if (!(ok = mbar_wait(&v_full[s], (t / kKVStages) & 1, status))) break;
         tc_fence_after();
         const uint64_t v = sw128_mnmajor_desc(smem_u32(sV + s * kKVBytes));
         const uint32_t pa = tmem + kColS + 64 * (t & 1);
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k)
-          tc_mma_f16_ts(tmem + kColO, pa + 8 * k, v + 128 * k, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-        tc_commit(o_done);
+          tc_mma_f16_ts(tmem + kColO, pa + 8 * k, v + 128 * k, idesc_pv, (cp.j > 0 || k > 0) ? 1u : 0u);
+        tc_commit(&o_done[t & 1]);
         tc_commit(&v_empty[s]);
-        if (t + 2 < n_steps) ok = issue_s(t + 2);  // S buffer t % 2 is free again
+        cp.advance(il);
+        if (cs.valid(il)) ok = issue_s();  // S buffer t % 2 is free again
       }
     }
   } else {
@@ -316,13 +385,11 @@ __global__ void __launch_bounds__(kThreads)
     const int st = threadIdx.x - 64;  // 0..127
     const int qd = warp & 3;          // TMEM lane quarter
     const int r = qd * 32 + lane;     // query row within the tile
-    const int qi = q0 + r;
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-    float m_run = -INFINITY, l_run = 0.f;
-    // Q of head hq: shared memory (TMA, 128-B swizzle) -> this thread's row
-    // of TMEM Q buffer hq % 2, then release the shared buffer.
-    auto stage_q = [&](int hq) -> bool {
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(q_full, hq & 1, status))) return false;
+    // Q of the g-th active item: shared memory (TMA, 128-B swizzle) -> this
+    // thread's row of TMEM Q buffer g % 2, then release the shared buffer.
+    auto stage_q = [&](int g) -> bool {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(q_full, g & 1, status))) return false;
       uint32_t qr[32];
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -332,164 +399,152 @@ __global__ void __launch_bounds__(kThreads)
         qr[4 * c + 2] = w.z;
         qr[4 * c + 3] = w.w;
       }
-      tmem_st_u32_x32(trow + kColQ + 32 * (hq & 1), qr);
+      tmem_st_u32_x32(trow + kColQ + 32 * (g & 1), qr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(q_empty);
-        mbar_arrive(&q_tm[hq & 1]);
+        mbar_arrive(&q_tm[g & 1]);
       }
       return true;
     };
-    bool ok = stage_q(0);
-    // Every step passes the named barrier, even after a failed wait, so a
-    // timed-out warp can never strand the other softmax warps there.
-    for (int t = 0; t < n_steps; ++t) {
-      const int hh = t / n_kt, j = t % n_kt;
-      const int k0 = j * kKeys;
-      if (j == 0) {
-        m_run = -INFINITY;
-        l_run = 0.f;
-        // one head ahead: Q buffer (hh + 1) % 2 last served head hh - 1,
-        // whose S tiles this thread has all consumed
-        if (ok && hh + 1 < nh) ok = stage_q(hh + 1);
+    bool ok = true;
+    int t = 0, g = 0;
+    for (int round = 0;; ++round) {
+      const Item it = il.decode(round);
+      if (it.id >= il.n_items) break;
+      const size_t row0 = static_cast<size_t>(it.b) * L;
+      const int qi = it.q0 + r;
+      // Every item passes the named barriers, even after a failed wait, so a
+      // timed-out warp can never strand the other softmax warps there.
+      if (it.q0 >= it.len) {
+        // every query row of this item is padding: zero output rows
+        if (qi < L) {
+          uint4* dst = reinterpret_cast<uint4*>(out + (row0 + qi) * inner + it.h * kDh);
+#pragma unroll
+          for (int c = 0; c < kDh / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
+        }
+        continue;
       }
-      // bias window of this step: win[e] for key - query = k0 - q0 - (kQ - 1) + e
-      // and win1[e] = win[e + 1]
-      float* win = sWin + (t & 1) * 2 * kWinPad;
-      float* win1 = win + kWinPad;
-      const float* tab = sTab + hh * 64;
-#ifdef WC_ATTN_TRACE
-      const unsigned long long ta = clock64();
-#endif
-      for (int e = st; e < kWin; e += 128) {
-        const float w = tab[sBkt[k0 + e]];
-        win[e] = w;
-        if (e > 0) win1[e - 1] = w;
+      if (g == 0 && ok) ok = stage_q(0);
+      // one item ahead: Q buffer (g + 1) % 2 last served item g - 1, whose
+      // S tiles this thread has all consumed
+      if (ok && il.next_active(round + 1).id < il.n_items) ok = stage_q(g + 1);
+      // bias row of this item (after every softmax thread has finished the
+      // previous one's steps)
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      {
+        const float* tab = sTab + it.h * 64;
+        for (int x = st; x < it.n_kt * kKeys + kWin; x += 128) {
+          const float w = tab[rel_bucket_tc(sThr, bt.half, x - it.q0 - (kQ - 1))];
+          sBias[x] = w;
+          if (x > 0) sBias[kBiasPad + x - 1] = w;
+        }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      // bias of key k0 + c at brow[c], brow 8-byte aligned
-      const float* brow = ((kQ - 1 - r) & 1) ? win1 + (kQ - 2 - r) : win + (kQ - 1 - r);
-#ifdef WC_ATTN_TRACE
-      const unsigned long long tb = clock64();
-      ATTN_TRACE_ADD(5, tb - ta);
-#endif
-      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[t & 1], (t >> 1) & 1, status));
-#ifdef WC_ATTN_TRACE
-      const unsigned long long tc = clock64();
-      ATTN_TRACE_ADD(4, tc - tb);
-      if (t == 0) ATTN_TRACE(2, tc);
-#endif
-      if (ok) {
-        tc_fence_after();
-        float v[kKeys];
-        tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1), &v[0]);
-        tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1) + 32, &v[32]);
-        tmem_wait_ld();
-        // v = S log2(e) + bias, two lanes per instruction; 4 max chains
-        const uint64_t kLog2e2 = f2(1.4426950408889634f, 1.4426950408889634f);
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int i = 0; i < kKeys; i += 2) {
-          const float2 bb = *reinterpret_cast<const float2*>(brow + i);
-          const uint64_t x = f2_fma(f2(v[i], v[i + 1]), kLog2e2, f2(bb.x, bb.y));
-          v[i] = f2_lo(x);
-          v[i + 1] = f2_hi(x);
-        }
-        if (k0 + kKeys > len) {
-#pragma unroll
-          for (int i = 0; i < kKeys; ++i)
-            if (k0 + i >= len) v[i] = -INFINITY;
-        }
-#pragma unroll
-        for (int i = 0; i < kKeys; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], v[i], v[i + 1]);
-        const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-        // Lazy rescale: keep the running max unless this tile raises it by
-        // more than 8 (log2 units), so P stays <= 2^8 and O is rescaled
-        // rarely; the final division by the matching sum makes it exact.
-        const float m_new = (tmax > m_run + 8.0f) ? tmax : m_run;
-        const float corr = ex2(m_run - m_new);  // 1 when kept, 0 on the head's first tile
-        // p = 2^(t - max) -> f16 P row over the first 32 columns of S buffer
-        // t % 2 (S(t) is in registers), row sum in f32
-        const uint64_t negm = f2(-m_new, -m_new);
-        uint64_t ps[4] = {0, 0, 0, 0};  // (+0, +0) pairs
-        uint32_t pk[kKeys / 2];
-#pragma unroll
-        for (int i = 0; i < kKeys; i += 2) {
-          const uint64_t x = f2_add(f2(v[i], v[i + 1]), negm);
-          const uint64_t p = f2(ex2(f2_lo(x)), ex2(f2_hi(x)));
-          ps[(i >> 1) & 3] = f2_add(ps[(i >> 1) & 3], p);
-          pk[i >> 1] = f2_to_h2(p);
-        }
-        tmem_st_u32_x32(trow + kColS + 64 * (t & 1), pk);
-        const uint64_t ps2 = f2_add(f2_add(ps[0], ps[1]), f2_add(ps[2], ps[3]));
-        const float psum = f2_lo(ps2) + f2_hi(ps2);
-        l_run = l_run * corr + psum;
-        m_run = m_new;
-        if (j > 0 && __any_sync(0xFFFFFFFFu, corr != 1.0f)) {
-          // O holds P(t-1) V(t-1) of this head once o_done says so; rescale it
-          // to the new max (rare with the lazy rule above)
-          ok = __all_sync(0xFFFFFFFFu, mbar_wait(o_done, (t - 1) & 1, status));
-          if (ok) {
-            tc_fence_after();
-            const uint32_t ocol = trow + kColO;
-#pragma unroll 1
-            for (int c = 0; c < kDh; c += 32) {
-              float o[32];
-              tmem_ld_32x32b_x32(ocol + c, o);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= corr;
-              tmem_st_32x32b_x32(ocol + c, o);
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-#ifdef WC_ATTN_TRACE
-      const unsigned long long td = clock64();
-      ATTN_TRACE_ADD(9, td - tc);
-#endif
-      if (j == n_kt - 1) {
-        // epilogue of head h: O / l -> f16, then release the O buffer
-        if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(o_done, t & 1, status));
-#ifdef WC_ATTN_TRACE
-        ATTN_TRACE_ADD(6, clock64() - td);
-#endif
+      // bias of key c at brow[c], brow 8-byte aligned
+      const float* brow = ((kQ - 1 - r) & 1) ? sBias + kBiasPad + (kQ - 2 - r) : sBias + (kQ - 1 - r);
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < it.n_kt; ++j, ++t) {
+        const int k0 = j * kKeys;
+        if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[t & 1], (t >> 1) & 1, status));
         if (ok) {
           tc_fence_after();
-          const float inv = 1.0f / l_run;
-          const uint32_t ocol = trow + kColO;
-#pragma unroll 1
-          for (int c = 0; c < kDh; c += 32) {
-            float o[32];
-            tmem_ld_32x32b_x32(ocol + c, o);
-            if (qi < L) {
-              __half* dst = out + (row0 + qi) * inner + (h0 + hh) * kDh + c;
+          float v[kKeys];
+          tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1), &v[0]);
+          tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1) + 32, &v[32]);
+          tmem_wait_ld();
+          // v = S log2(e) + bias, two lanes per instruction; 4 max chains
+          const uint64_t kLog2e2 = f2(1.4426950408889634f, 1.4426950408889634f);
+          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 w;
-                w.x = pack_f16x2_sat(o[i] * inv, o[i + 1] * inv);
-                w.y = pack_f16x2_sat(o[i + 2] * inv, o[i + 3] * inv);
-                w.z = pack_f16x2_sat(o[i + 4] * inv, o[i + 5] * inv);
-                w.w = pack_f16x2_sat(o[i + 6] * inv, o[i + 7] * inv);
-                *reinterpret_cast<uint4*>(dst + i) = w;
+          for (int i = 0; i < kKeys; i += 2) {
+            const float2 bb = *reinterpret_cast<const float2*>(brow + k0 + i);
+            const uint64_t x = f2_fma(f2(v[i], v[i + 1]), kLog2e2, f2(bb.x, bb.y));
+            v[i] = f2_lo(x);
+            v[i + 1] = f2_hi(x);
+          }
+          if (k0 + kKeys > it.len) {
+#pragma unroll
+            for (int i = 0; i < kKeys; ++i)
+              if (k0 + i >= it.len) v[i] = -INFINITY;
+          }
+#pragma unroll
+          for (int i = 0; i < kKeys; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], v[i], v[i + 1]);
+          const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+          // Lazy rescale: keep the running max unless this tile raises it by
+          // more than 8 (log2 units), so P stays <= 2^8 and O is rescaled
+          // rarely; the final division by the matching sum makes it exact.
+          const float m_new = (tmax > m_run + 8.0f) ? tmax : m_run;
+          const float corr = ex2(m_run - m_new);  // 1 when kept, 0 on the item's first tile
+          // p = 2^(v - max) -> f16 P row over the first 32 columns of S buffer
+          // t % 2 (S(t) is in registers), row sum in f32
+          const uint64_t negm = f2(-m_new, -m_new);
+          uint64_t ps[4] = {0, 0, 0, 0};  // (+0, +0) pairs
+          uint32_t pk[kKeys / 2];
+#pragma unroll
+          for (int i = 0; i < kKeys; i += 2) {
+            const uint64_t x = f2_add(f2(v[i], v[i + 1]), negm);
+            const uint64_t p = f2(ex2(f2_lo(x)), ex2(f2_hi(x)));
+            ps[(i >> 1) & 3] = f2_add(ps[(i >> 1) & 3], p);
+            pk[i >> 1] = f2_to_h2(p);
+          }
+          tmem_st_u32_x32(trow + kColS + 64 * (t & 1), pk);
+          const uint64_t ps2 = f2_add(f2_add(ps[0], ps[1]), f2_add(ps[2], ps[3]));
+          const float psum = f2_lo(ps2) + f2_hi(ps2);
+          l_run = l_run * corr + psum;
+          m_run = m_new;
+          if (j > 0 && __any_sync(0xFFFFFFFFu, corr != 1.0f)) {
+            // O holds P(t-1) V(t-1) of this item once o_done says so; rescale
+            // it to the new max (rare with the lazy rule above)
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, status));
+            if (ok) {
+              tc_fence_after();
+              const uint32_t ocol = trow + kColO;
+#pragma unroll 1
+              for (int c = 0; c < kDh; c += 32) {
+                float o[32];
+                tmem_ld_32x32b_x32(ocol + c, o);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] *= corr;
+                tmem_st_32x32b_x32(ocol + c, o);
               }
             }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t & 1]);
       }
+      // epilogue of the item: O / l -> f16 (the next P V overwrites O only
+      // after this thread's next arrival on p_full)
+      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, status));
+      if (ok) {
+        tc_fence_after();
+        const float inv = 1.0f / l_run;
+        const uint32_t ocol = trow + kColO;
+#pragma unroll 1
+        for (int c = 0; c < kDh; c += 32) {
+          float o[32];
+          tmem_ld_32x32b_x32(ocol + c, o);
+          if (qi < L) {
+            __half* dst = out + (row0 + qi) * inner + it.h * kDh + c;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w;
+              w.x = pack_f16x2_sat(o[i] * inv, o[i + 1] * inv);
+              w.y = pack_f16x2_sat(o[i + 2] * inv, o[i + 3] * inv);
+              w.z = pack_f16x2_sat(o[i + 4] * inv, o[i + 5] * inv);
+              w.w = pack_f16x2_sat(o[i + 6] * inv, o[i + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + i) = w;
+            }
+          }
+        }
+      }
+      ++g;
     }
   }
 
-  ATTN_TRACE(3, clock64());
-#ifdef WC_ATTN_TRACE
-  ATTN_TRACE(4, tr_acc[4]);
-  ATTN_TRACE(5, tr_acc[5]);
-  ATTN_TRACE(6, tr_acc[6]);
-  ATTN_TRACE(9, tr_acc[9]);
-#endif
   __syncwarp();
   tc_fence_before();
   __syncthreads();
@@ -501,40 +556,27 @@ __global__ void __launch_bounds__(kThreads)
 
 }  // namespace
 
-#ifdef WC_ATTN_TRACE
-extern "C" int wc_debug_attn_trace(unsigned long long* host, int n_ctas) {
-  return cudaMemcpyFromSymbol(host, g_attn_trace, sizeof(unsigned long long) * kTraceSlots *
-                                                      (n_ctas < kTraceCtas ? n_ctas : kTraceCtas)) == cudaSuccess ? 0 : -4;
-}
-#endif
-
 cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const int32_t* lengths, int B, int L, int H,
                                 const float* bias_tab, const BucketThresholds& bt, uint32_t* status,
                                 cudaStream_t st) {
   if (B <= 0 || L <= 0) return cudaSuccess;
-  if (L > kMaxL || 2 * bt.half > 64) return cudaErrorInvalidValue;
+  if (L > kMaxL || 2 * bt.half > 64 || H <= 0 || H > kMaxHeads) return cudaErrorInvalidValue;
+  const int64_t n_items = static_cast<int64_t>((L + kQ - 1) / kQ) * B * H;
+  if (n_items > INT32_MAX || static_cast<int64_t>(B) * L > INT32_MAX) return cudaErrorInvalidValue;
   static bool attr_set[64] = {};
+  static int num_sms[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  // Heads per CTA: a CTA walks (head, key tile) steps as one pipeline, so
-  // short sequences take several heads per CTA to amortise its set-up, long
-  // ones one head (more, shorter CTAs balance the waves better); measured on
-  // B200 at L = 32, 182 and 512.
-  const int q_tiles = (L + kQ - 1) / kQ;
-  int hpc = std::min(std::min(H, kMaxHeads), std::max(1, (256 + L - 1) / L));
-  // ... but never fewer than about two CTAs per SM while heads can be split
-  while (hpc > 1 && static_cast<int64_t>(q_tiles) * B * ((H + hpc - 1) / hpc) < 2 * 148) --hpc;
-  const int groups = (H + hpc - 1) / hpc;
-  hpc = (H + groups - 1) / groups;  // balance the groups
-  dim3 grid(q_tiles, groups, B);
-  return launch_pdl(attention_tc_kernel, grid, dim3(kThreads), kSmem, st, nullptr, 0, tm_qkv, out, lengths, L, H, hpc,
-                    bias_tab, bt, status);
+  const int grid = static_cast<int>(std::min<int64_t>(n_items, static_cast<int64_t>(kCtasPerSm) * num_sms[dev]));
+  return launch_pdl(attention_tc_kernel, dim3(grid), dim3(kThreads), kSmem, st, nullptr, 0, tm_qkv, out, lengths, B, L,
+                    H, bias_tab, bt, status);
 }
 
 }  // namespace wc
