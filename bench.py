@@ -42,7 +42,7 @@ MAX_BATCH_TOKENS = 16384
 LAUNCHES_PER_FORWARD_PER_LAYER = 7   # qkv gemm, attention, o gemm, rmsnorm, wi gemm, wo gemm, rmsnorm
 # dram read+write bytes per launch of the dominant kernel from the committed ncu
 # capture at M = 16,384.
-NCU_TRAFFIC_BYTES = 41278464  # 26.98 MB read + 14.30 MB written, profiles/gemm2_geglu_m16384.md
+NCU_TRAFFIC_BYTES = 49470720  # 31.49 MB read + 17.98 MB written, profiles/gemm2_geglu_f16_m16384.md
 
 
 def _peaks():
@@ -342,10 +342,11 @@ def _time_launches(fn, stream, reps: int, warm: int = 3) -> float:
 
 
 def kernel_measurements(enc, args, peak, peak_src):
-    """Per-kernel timings for the roofline: the gated-GELU Q4_K GEMM (the
-    dominant kernel, 44% of encoder FLOPs) at one full batch (M = 16,384),
-    plus the other GEMM shapes (config 2, M = 8192) and attention (config 3),
-    each timed with CUDA events on its launch stream."""
+    """Per-kernel timings for the roofline: the gated-GELU GEMM (the dominant
+    kernel, 44% of encoder FLOPs) at one full batch (M = 16,384) on the
+    resident f16 weights the forward uses from 512 rows, plus the other GEMM
+    shapes (config 2, M = 8192; the fused-dequant Q4_K kernel for comparison)
+    and attention (config 3), each timed with CUDA events on its launch stream."""
     import torch
     from witchcraft_b200._lib import check, lib
     from witchcraft_b200.synth import quantize_q4k
@@ -356,31 +357,39 @@ def kernel_measurements(enc, args, peak, peak_src):
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
     def wq(n, k):
-        return torch.from_numpy(quantize_q4k(rng.standard_normal((n, k)).astype(np.float32) * 0.02).reshape(-1)).cuda()
+        """(Q4_K bytes, the same weights dequantised to f16 [n][k])"""
+        q = torch.from_numpy(quantize_q4k(rng.standard_normal((n, k)).astype(np.float32) * 0.02).reshape(-1)).cuda()
+        h = torch.empty(n, k, device="cuda", dtype=torch.float16)
+        check(l.wc_q4k_dequant_f16(P(q), q.numel() // 144, P(h), sp))
+        return q, h
 
-    out = {}
     w0, w1 = wq(2048, 768), wq(2048, 768)
-    wqkv, wo = wq(2304, 768), wq(768, 2048)
+    wqkv, wo, wattn = wq(2304, 768), wq(768, 2048), wq(768, 768)
 
-    def gemm_case(M, K, N, epi, w, wu):
+    def gemm_case(M, K, N, epi, w, wu, fused_q4k=False):
         x = torch.randn(M, K, device="cuda").half()
         y = torch.empty(M, N, device="cuda", dtype=torch.float16 if epi in (0, 1) else torch.float32)
-        f = lambda: check(l.wc_gemm_q4k(P(x), M, K, P(w), P(wu) if wu is not None else None, N, epi, P(y), sp))  # noqa
+        k = 0 if fused_q4k else 1
+        fn = l.wc_gemm_q4k if fused_q4k else l.wc_gemm_f16
+        f = lambda: check(fn(P(x), M, K, P(w[k]), P(wu[k]) if wu is not None else None, N, epi, P(y), sp))  # noqa
         t = _time_launches(f, st, reps=20)
         flops = 2.0 * M * K * N * (2 if epi == 1 else 1)
         return t, flops
 
     t, fl = gemm_case(16384, 768, 2048, 1, w0, w1)
     achieved = fl / t / 1e12
-    roof = {"bound": "tensor", "kernel": "gemm2_q4k_kernel<kEpiGeGLU> (wi_0|wi_1 + gated GELU, 2-SM), M=16384 K=768 N=2x2048",
+    roof = {"bound": "tensor",
+            "kernel": "gemm2_q4k_kernel<kEpiGeGLU, f16 weights> (wi_0|wi_1 + gated GELU, 2-SM), M=16384 K=768 N=2x2048",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_source": f"{peak_src} dense bf16/f16 burst", "traffic": NCU_TRAFFIC_BYTES,
             "avg_launch_us": t * 1e6, "algorithmic_flop_per_launch": fl}
     micro = {}
-    for name, (M, K, N, epi, w, wu) in {"qkv_M8192": (8192, 768, 2304, 0, wqkv, None),
-                                        "wi_geglu_M8192": (8192, 768, 2048, 1, w0, w1),
-                                        "wo_M8192": (8192, 2048, 768, 3, wo, None)}.items():
-        t, fl = gemm_case(M, K, N, epi, w, wu)
+    for name, (M, K, N, epi, w, wu, fq) in {"qkv_M8192": (8192, 768, 2304, 0, wqkv, None, False),
+                                            "wi_geglu_M8192": (8192, 768, 2048, 1, w0, w1, False),
+                                            "wo_M8192": (8192, 2048, 768, 3, wo, None, False),
+                                            "o_M8192": (8192, 768, 768, 3, wattn, None, False),
+                                            "wi_geglu_M8192_fused_q4k": (8192, 768, 2048, 1, w0, w1, True)}.items():
+        t, fl = gemm_case(M, K, N, epi, w, wu, fq)
         micro[name] = {"us": t * 1e6, "tflops": fl / t / 1e12, "frac_of_peak": fl / t / 1e12 / peak}
     # attention, config 3
     B, L, H = 64, 512, 12
@@ -421,8 +430,10 @@ def query_latency(enc, runs: int = 200):
     return res
 
 
-def profile_kernel(name: str, m: int, launches: int = 5):
-    """A few launches of one kernel (for an ncu capture of that kernel alone)."""
+def profile_kernel(name: str, m: int, launches: int = 5, fused_q4k: bool = False):
+    """A few launches of one kernel (for an ncu capture of that kernel alone):
+    the GEMMs on f16 weights as the forward runs them, or with fused_q4k the
+    Q4_K-dequantising variant."""
     import torch
     from witchcraft_b200._lib import check, lib
     from witchcraft_b200.synth import quantize_q4k
@@ -431,7 +442,12 @@ def profile_kernel(name: str, m: int, launches: int = 5):
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
     def wq(n, k):
-        return torch.from_numpy(quantize_q4k(rng.standard_normal((n, k)).astype(np.float32) * 0.02).reshape(-1)).cuda()
+        q = torch.from_numpy(quantize_q4k(rng.standard_normal((n, k)).astype(np.float32) * 0.02).reshape(-1)).cuda()
+        if fused_q4k:
+            return q
+        h = torch.empty(n, k, device="cuda", dtype=torch.float16)
+        check(l.wc_q4k_dequant_f16(P(q), q.numel() // 144, P(h), None))
+        return h
     if name == "attention":
         B, L, H = 64, 512, 12
         lens = torch.from_numpy(np.random.default_rng(4).integers(32, 513, B).astype(np.int32)).cuda()
@@ -444,7 +460,8 @@ def profile_kernel(name: str, m: int, launches: int = 5):
         w, wu = wq(N, K), (wq(N, K) if epi == 1 else None)
         x = torch.randn(m, K, device="cuda").half()
         y = torch.zeros(m, N, device="cuda", dtype=torch.float16 if epi in (0, 1) else torch.float32)
-        f = lambda: check(l.wc_gemm_q4k(P(x), m, K, P(w), P(wu) if wu is not None else None, N, epi, P(y), None))  # noqa: E731
+        fn = l.wc_gemm_q4k if fused_q4k else l.wc_gemm_f16
+        f = lambda: check(fn(P(x), m, K, P(w), P(wu) if wu is not None else None, N, epi, P(y), None))  # noqa: E731
     for _ in range(launches):
         f()
     torch.cuda.synchronize()
@@ -464,9 +481,10 @@ def main():
     ap.add_argument("--profile-kernel", choices=["geglu", "qkv", "wo", "attention"], default=None,
                     help="only launch one kernel a few times (for ncu)")
     ap.add_argument("--m", type=int, default=16384, help="GEMM rows for --profile-kernel")
+    ap.add_argument("--fused-q4k", action="store_true", help="--profile-kernel: the Q4_K-dequantising GEMM")
     args = ap.parse_args()
     if args.profile_kernel:
-        profile_kernel(args.profile_kernel, args.m)
+        profile_kernel(args.profile_kernel, args.m, fused_q4k=args.fused_q4k)
         return
     if args.impl == "reference":
         run_reference(args)

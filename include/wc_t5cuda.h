@@ -117,6 +117,11 @@ int wc_t5_dims(const wc_t5* h, int* d_model, int* n_layers, int* d_proj, int* vo
  * k_quants BlockQ4K as used at src/quantized_t5.rs:44). */
 int wc_q4k_dequant(const void* d_blocks, int64_t nblocks, float* d_out, void* stream);
 
+/* The same values rounded to f16 (nearest even): the resident weight copies
+ * that the large-M GEMMs of wc_t5_forward read (the reference dequantises at
+ * load too, src/quantized_t5.rs:44). */
+int wc_q4k_dequant_f16(const void* d_blocks, int64_t nblocks, void* d_out_f16, void* stream);
+
 /* Y = X . W^T with X f16 [M][K] and W Q4_K [N][K/256 blocks]
  * (QMatMul::forward, src/quantized_t5.rs:39-49; QTiledOp, src/fused_matmul.rs:46-59).
  * epilogue: 0 = f16 out [M][N]; 1 = gated GELU: gelu_tanh(X.W^T) * (X.W_up^T)
@@ -126,6 +131,13 @@ int wc_q4k_dequant(const void* d_blocks, int64_t nblocks, float* d_out, void* st
  *           3 = f32 out [M][N].
  * K % 256 == 0, N % 128 == 0, M >= 1. */
 int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const void* d_w_up, int N, int epilogue,
+                void* d_out, void* stream);
+
+/* The same GEMM and epilogues with W already dequantised to f16 [N][K]
+ * (wc_q4k_dequant_f16): the kernel wc_t5_forward runs for batches of 512
+ * rows and more (the 2-SM persistent GEMM).  K % 256 == 0, N % 256 == 0
+ * (N % 128 == 0 for the gated GELU), M >= 1. */
+int wc_gemm_f16(const void* d_x, int M, int K, const void* d_w_f16, const void* d_w_up_f16, int N, int epilogue,
                 void* d_out, void* stream);
 
 /* Encoder self-attention (src/quantized_t5.rs:426-500) over a padded batch.

@@ -13,7 +13,7 @@ from oracle import oracle as O
 from witchcraft_b200._lib import check, lib
 from witchcraft_b200.synth import quantize_q4k
 
-from gpu_util import dequant_gpu, dptr, gemm_gpu, stream_ptr
+from gpu_util import dequant_gpu, dptr, gemm_gpu, q4k_to_device, stream_ptr
 
 pytestmark = pytest.mark.gpu
 
@@ -33,6 +33,25 @@ def test_dequant_bit_exact_against_golden():
 def test_dequant_bit_exact_full_embedding_table(xtr_model):
     blocks = xtr_model.q4k["encoder.embed_tokens.weight"]
     assert _same_bits(dequant_gpu(blocks).cpu().numpy(), O.q4k_dequant(blocks))
+
+
+def test_dequant_f16_is_rounded_f32_dequant(xtr_model):
+    """The resident f16 weights equal the bit-exact f32 dequant rounded to f16."""
+    g = np.load(os.path.join(GOLDEN, "q4k_golden.npz"))
+    for blocks, ref32 in [(g["blocks"], g["values"]),
+                          (xtr_model.q4k["encoder.block.0.layer.1.DenseReluDense.wi_0.weight"], None)]:
+        if ref32 is None:
+            ref32 = O.q4k_dequant(blocks)
+        d = q4k_to_device(blocks)
+        n = d.numel() // 144
+        out = torch.empty(n * 256, dtype=torch.float16, device="cuda")
+        check(lib().wc_q4k_dequant_f16(dptr(d), n, dptr(out), stream_ptr()))
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        want = np.asarray(ref32, np.float32).reshape(-1).astype(np.float16)
+        nan = np.isnan(want)
+        assert np.array_equal(np.isnan(got), nan)
+        assert np.array_equal(got[~nan].view(np.uint16), want[~nan].view(np.uint16))
 
 
 def _gelu(g):
@@ -91,6 +110,49 @@ def test_gemm_residual_accumulates(M):
     gemm_gpu(x, blocks, 2, out=out)
     ref = base + x.float() @ wd.to(torch.float16).float().T
     assert ((out - ref).abs().max() / ref.abs().max()).item() < 2e-3
+
+
+def _dequant_f16(blocks):
+    d = q4k_to_device(blocks)
+    out = torch.empty(blocks.shape[0], blocks.shape[1] * 256, dtype=torch.float16, device="cuda")
+    check(lib().wc_q4k_dequant_f16(dptr(d), d.numel() // 144, dptr(out), stream_ptr()))
+    return out
+
+
+def _gemm_f16_gpu(x16, w16, epi, w_up16=None, out=None):
+    M, K = x16.shape
+    N = w16.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float16 if epi in (0, 1) else torch.float32, device="cuda")
+    check(lib().wc_gemm_f16(dptr(x16), M, K, dptr(w16), dptr(w_up16) if w_up16 is not None else None, N, epi,
+                            dptr(out), stream_ptr()))
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("M", [8192, 1300, 300, 1])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_gemm_f16_weights(M, epi):
+    """The forward's large-M GEMM on resident f16 weights: bitwise equal to the
+    fused-dequant kernel where both run the 2-SM kernel (M >= 512), and within
+    the GEMM tolerance of fp32 torch on the same operands everywhere."""
+    K, N = (2048, 768) if epi in (2, 3) else (768, 512)
+    b0, w0 = _weights(N, K, 20 + epi)
+    b1, w1 = _weights(N, K, 30 + epi)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(4)).cuda().to(torch.float16)
+    h0, h1 = _dequant_f16(b0), _dequant_f16(b1)
+    base = torch.randn(M, N, generator=torch.Generator().manual_seed(5)).cuda() if epi == 2 else None
+    y16 = _gemm_f16_gpu(x, h0, epi, h1 if epi == 1 else None, base.clone() if base is not None else None)
+    xf = x.float()
+    if epi == 1:
+        ref = _gelu(xf @ h0.float().T) * (xf @ h1.float().T)
+    else:
+        ref = xf @ h0.float().T + (base if epi == 2 else 0)
+    assert ((y16.float() - ref).abs().max() / ref.abs().max()).item() < 5e-3
+    if M >= 512:
+        yq = gemm_gpu(x, b0, epi, w_up_blocks=b1 if epi == 1 else None,
+                      out=base.clone() if base is not None else None)
+        assert torch.equal(y16, yq)
 
 
 def test_gemm_rejects_bad_shapes():

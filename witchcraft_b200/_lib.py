@@ -35,7 +35,9 @@ _SIGNATURES = {
     "wc_t5_sync": (c_int, [c_void_p, c_void_p]),
     "wc_t5_dims": (c_int, [c_void_p, _P(c_int), _P(c_int), _P(c_int), _P(c_int)]),
     "wc_q4k_dequant": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
+    "wc_q4k_dequant_f16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     "wc_gemm_q4k": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "wc_gemm_f16": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "wc_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "wc_t5_relative_bucket": (c_int, [c_int, c_int, c_int, c_int]),
     "wc_selftest_wait_timeout": (c_int, [ctypes.c_uint64]),

@@ -28,6 +28,21 @@ __global__ void q4k_dequant_kernel(const uint8_t* __restrict__ blocks, int64_t n
   o[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
+// The same elements rounded to f16 (round to nearest even): the operand
+// values the fused-dequant GEMMs feed the tensor cores.
+__global__ void q4k_dequant_f16_kernel(const uint8_t* __restrict__ blocks, int64_t nblocks, __half* __restrict__ out) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t blk = gid >> 5;
+  if (blk >= nblocks) return;
+  const int e = static_cast<int>(gid & 31) * 8;
+  const uint8_t* p = blocks + blk * 144;
+  const Q4KScales s = q4k_load_scales(p);
+  float v[8];
+  q4k_block_elems8(p, s, e, v);
+  *reinterpret_cast<uint4*>(out + blk * 256 + e) =
+      make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]), pack_f16x2(v[6], v[7]));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -151,6 +166,14 @@ cudaError_t q4k_dequant_launch(const uint8_t* blocks, int64_t nblocks, float* ou
   const int64_t threads = nblocks * 32;
   const int bs = 256;
   q4k_dequant_kernel<<<static_cast<unsigned>((threads + bs - 1) / bs), bs, 0, st>>>(blocks, nblocks, out);
+  return cudaGetLastError();
+}
+
+cudaError_t q4k_dequant_f16_launch(const uint8_t* blocks, int64_t nblocks, __half* out, cudaStream_t st) {
+  if (nblocks <= 0) return cudaSuccess;
+  const int64_t threads = nblocks * 32;
+  const int bs = 256;
+  q4k_dequant_f16_kernel<<<static_cast<unsigned>((threads + bs - 1) / bs), bs, 0, st>>>(blocks, nblocks, out);
   return cudaGetLastError();
 }
 

@@ -9,6 +9,8 @@ namespace wc {
 
 // nblocks Q4_K super-blocks -> 256 * nblocks f32, bit-exact with the reference.
 cudaError_t q4k_dequant_launch(const uint8_t* blocks, int64_t nblocks, float* out, cudaStream_t st);
+// Same, rounded to f16 (round to nearest even).
+cudaError_t q4k_dequant_f16_launch(const uint8_t* blocks, int64_t nblocks, __half* out, cudaStream_t st);
 
 // x[m] = dequant(table row ids[m]) (id 0 for positions past a sequence's
 // valid length), xn[m] = f16(RMSNorm(x[m]) * w).  table: Q4_K [vocab][D/256].

@@ -24,6 +24,10 @@
 //   warps 2-9   dequant: raw Q4_K -> f16 K-major 128-B-swizzled B stages
 //   warps 10-13 epilogue: tcgen05.ld -> registers -> swizzled smem staging ->
 //               TMA tensor store (kEpiResid: TMA load of the x tile, add, TMA store)
+// With WF16 the weights are already f16 ([N][K], dequantised once from the
+// same Q4_K bytes with the same arithmetic, so the operands are bit-identical):
+// the producer TMA-loads each CTA's 128-row B half into the stage of its X
+// rows, both completing on the same barrier, and the dequant warps idle.
 // Cross-CTA signalling: X loads of both CTAs complete on the even CTA's
 // barrier; dequant and epilogue warps arrive on the even CTA's barriers
 // through shared::cluster addresses; MMA completion is committed to both
@@ -170,7 +174,7 @@ __device__ __forceinline__ uint4 dequant8_f16(uint32_t x0, uint32_t x1, uint64_t
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-template <int EPI>
+template <int EPI, bool WF16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_q4k_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
                      const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmOut,
@@ -249,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nt = tile % n_tiles;
         const int w_row0 = EPI == kEpiGeGLU ? nt * kHalfN : nt * kBN + static_cast<int>(rank) * kHalfN;
         for (int t = 0; t < ksteps; ++t) {
-          if ((t & 3) == 0) {
+          if (!WF16 && (t & 3) == 0) {
             const uint32_t sw = iw % kSW;
             if (!(ok = mbar_wait(&empty_w[sw], ((iw / kSW) & 1) ^ 1, p.status))) break;
             mbar_arrive_expect_tx(&full_w[sw], kWBytes);
@@ -258,8 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t sa = ia % kSA;
           if (!(ok = mbar_wait(&empty_a[sa], ((ia / kSA) & 1) ^ 1, p.status))) break;
-          if (leader) mbar_arrive_expect_tx(&full_a[sa], 2 * kABytes);
+          if (leader) mbar_arrive_expect_tx(&full_a[sa], WF16 ? 2 * (kABytes + kBBytes) : 2 * kABytes);
           tma_load_2d_pair(sA + sa * kABytes, &tmA, map_to_rank(&full_a[sa], 0), t * kBK, m0);
+          if (WF16)  // B stage sa holds this CTA's weight rows of the same K step
+            tma_load_2d_pair(sB + sa * kBBytes, wmap, map_to_rank(&full_a[sa], 0), t * kBK, w_row0);
           ++ia;
         }
       }
@@ -278,21 +284,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < ksteps; ++t, ++ia, ++ib) {
           const uint32_t sa = ia % kSA, sb = ib % kSB;
           ok = mbar_wait_cluster(&full_a[sa], (ia / kSA) & 1, p.status) &&
-               mbar_wait_cluster(&full_b[sb], (ib / kSB) & 1, p.status);
+               (WF16 || mbar_wait_cluster(&full_b[sb], (ib / kSB) & 1, p.status));
           if (!ok) break;
           tc_fence_after();
           const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + sa * kABytes));
-          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + sb * kBBytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + (WF16 ? sa : sb) * kBBytes));
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
             tc_mma_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (t > 0 || k > 0) ? 1u : 0u);
           tc_commit_pair(&empty_a[sa]);
-          tc_commit_pair(&empty_b[sb]);
+          if (!WF16) tc_commit_pair(&empty_b[sb]);
         }
         if (ok) tc_commit_pair(&acc_full[buf]);
       }
     }
   } else if (warp < 2 + kDequantWarps) {
+    if (WF16) {
+      // no dequant work: the weights arrive by TMA
+    } else {
     // ------------------------------------------------------------ dequant
     // The 4 B stages rotate over 4 pairs of warps: pair g dequantises every
     // K step with (step % 4) == g, i.e. the 64-wide slice g of each Q4_K
@@ -338,6 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_remote(full_b_leader);
         }
       }
+    }
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -480,15 +490,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int EPI>
+template <int EPI, bool WF16>
 cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& out,
                    const GemmParams& p, int num_sms, cudaStream_t st) {
+  static_assert(kSA == kSB, "with f16 weights the B stages follow the X stages");
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm2_q4k_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm2_q4k_kernel<EPI, WF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
@@ -499,7 +511,7 @@ cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMa
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  return launch_pdl(gemm2_q4k_kernel<EPI>, dim3(2 * clusters), dim3(kThreads), kSmem, st, attr, 1, a, w0, w1, out, p);
+  return launch_pdl(gemm2_q4k_kernel<EPI, WF16>, dim3(2 * clusters), dim3(kThreads), kSmem, st, attr, 1, a, w0, w1, out, p);
 }
 
 }  // namespace
@@ -510,12 +522,21 @@ bool gemm2_q4k_supports(int epi, int M, int N, int K) {
 }
 
 cudaError_t gemm2_q4k_launch(int epi, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
-                             const CUtensorMap& out, const GemmParams& p, int num_sms, cudaStream_t st) {
+                             const CUtensorMap& out, const GemmParams& p, int num_sms, cudaStream_t st, bool w_f16) {
+  if (w_f16) {
+    switch (epi) {
+      case kEpiF16: return launch<kEpiF16, true>(a, w0, w1, out, p, num_sms, st);
+      case kEpiGeGLU: return launch<kEpiGeGLU, true>(a, w0, w1, out, p, num_sms, st);
+      case kEpiResid: return launch<kEpiResid, true>(a, w0, w1, out, p, num_sms, st);
+      case kEpiF32: return launch<kEpiF32, true>(a, w0, w1, out, p, num_sms, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (epi) {
-    case kEpiF16: return launch<kEpiF16>(a, w0, w1, out, p, num_sms, st);
-    case kEpiGeGLU: return launch<kEpiGeGLU>(a, w0, w1, out, p, num_sms, st);
-    case kEpiResid: return launch<kEpiResid>(a, w0, w1, out, p, num_sms, st);
-    case kEpiF32: return launch<kEpiF32>(a, w0, w1, out, p, num_sms, st);
+    case kEpiF16: return launch<kEpiF16, false>(a, w0, w1, out, p, num_sms, st);
+    case kEpiGeGLU: return launch<kEpiGeGLU, false>(a, w0, w1, out, p, num_sms, st);
+    case kEpiResid: return launch<kEpiResid, false>(a, w0, w1, out, p, num_sms, st);
+    case kEpiF32: return launch<kEpiF32, false>(a, w0, w1, out, p, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -109,8 +109,10 @@ bool make_q4k_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K, ui
 struct LayerW {
   uint8_t *qkv, *o, *wi0, *wi1, *wo;
   float *ln0, *ln1;
-  CUtensorMap tm_qkv, tm_o, tm_wi0, tm_wi1, tm_wo;       // 1-SM kernel boxes
-  CUtensorMap tm2_qkv, tm2_o, tm2_wi0, tm2_wi1, tm2_wo;  // 2-SM kernel boxes
+  CUtensorMap tm_qkv, tm_o, tm_wi0, tm_wi1, tm_wo;  // 1-SM kernel boxes
+  // The same matrices dequantised once to f16 [N][K] (the large-M GEMMs)
+  __half *h_qkv, *h_o, *h_wi0, *h_wi1, *h_wo;
+  CUtensorMap tmh_qkv, tmh_o, tmh_wi0, tmh_wi1, tmh_wo;
 };
 
 // Rows from which the 2-SM persistent GEMM replaces the 1-SM kernel.
@@ -138,6 +140,7 @@ struct wc_t5 {
   int inner = 0, d_proj = 128;
   int bn_qkv = 0, bn_o = 0, bn_wi = 0, bn_wo = 0;
   uint8_t* arena = nullptr;  // all weights, one allocation
+  __half* arena_f16 = nullptr;  // the layer matrices dequantised to f16, one allocation
   uint8_t* embed = nullptr;
   uint8_t* proj = nullptr;
   float* final_ln = nullptr;
@@ -261,7 +264,8 @@ int gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0,
   return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
 }
 
-// Layer GEMM: the 2-SM persistent kernel for large M, else the 1-SM kernel.
+// Layer GEMM: the 2-SM persistent kernel for large M (on the resident f16
+// weights, w0_2 / w1_2), else the 1-SM kernel on the Q4_K rows.
 // Up to kGemvMaxRows rows the small-M kernel (all SMs stream the weights once)
 // runs instead; it reads the activations and the raw weights by pointer.
 int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
@@ -283,7 +287,7 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
     CUtensorMap tm_out;
     if (!make_out_map(&tm_out, out, M, ldo, epi == kEpiF32 || epi == kEpiResid))
       return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a GEMM output");
-    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, device_sm_count(h->device), st);
+    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, device_sm_count(h->device), st, true);
     return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
   }
   return gemm(h, epi, bn, a, w0, w1, M, N, K, out, ldo, st);
@@ -310,16 +314,16 @@ int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B,
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, h->qkv, 3 * I, st, h->xn, w.qkv, w.qkv)))
+    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, w.tmh_qkv, w.tmh_qkv, M, 3 * I, D, h->qkv, 3 * I, st, h->xn, w.qkv, w.qkv)))
       return rc;
     if ((e = attention_tc_launch(tm_qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) !=
         cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, res_epi, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, res_out, D, st, h->att, w.o, w.o))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tmh_o, w.tmh_o, M, D, I, res_out, D, st, h->att, w.o, w.o))) return rc;
     if ((e = rmsnorm_launch(h->x, res_delta, w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
-    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, h->hbuf, F, st, h->xn, w.wi0, w.wi1))) return rc;
-    if ((rc = layer_gemm(h, res_epi, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, res_out, D, st, h->hbuf, w.wo, w.wo))) return rc;
+    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tmh_wi0, w.tmh_wi1, M, 2 * F, D, h->hbuf, F, st, h->xn, w.wi0, w.wi1))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tmh_wo, w.tmh_wo, M, D, F, res_out, D, st, h->hbuf, w.wo, w.wo))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(h->x, res_delta, next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
       return cuda_fail(h, e, "rmsnorm launch");
@@ -415,6 +419,7 @@ extern "C" int wc_t5_destroy(wc_t5* h) {
     if (h->stream) cudaStreamSynchronize(h->stream);
     free_workspace(h);
     if (h->arena) cudaFree(h->arena);
+    if (h->arena_f16) cudaFree(h->arena_f16);
     if (h->d_status) cudaFree(h->d_status);
     if (h->stream) cudaStreamDestroy(h->stream);
   }
@@ -612,16 +617,44 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
          make_q4k_map(&w.tm_o, w.o, D, I, gemm_q4k_w_box_rows(kEpiF32, h->bn_o)) &&
          make_q4k_map(&w.tm_wi0, w.wi0, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
          make_q4k_map(&w.tm_wi1, w.wi1, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
-         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiF32, h->bn_wo)) &&
-         make_q4k_map(&w.tm2_qkv, w.qkv, 3 * I, D, kGemm2WBoxRows) &&
-         make_q4k_map(&w.tm2_o, w.o, D, I, kGemm2WBoxRows) &&
-         make_q4k_map(&w.tm2_wi0, w.wi0, F, D, kGemm2WBoxRows) &&
-         make_q4k_map(&w.tm2_wi1, w.wi1, F, D, kGemm2WBoxRows) &&
-         make_q4k_map(&w.tm2_wo, w.wo, D, F, kGemm2WBoxRows);
+         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiF32, h->bn_wo));
   }
   if (!ok) {
     wc_t5_destroy(h);
     return fail(nullptr, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a weight tensor");
+  }
+  // Resident f16 copies of the layer matrices for the large-M GEMMs: the
+  // reference dequantises its Q4_K weights once at load, and so does this,
+  // with the rounding to f16 the fused-dequant kernels apply to their operands.
+  {
+    const int64_t per_layer = (3 * static_cast<int64_t>(I) * D + static_cast<int64_t>(D) * I +
+                               2 * static_cast<int64_t>(F) * D + static_cast<int64_t>(D) * F);
+    if ((e = cudaMalloc(&h->arena_f16, per_layer * cfg.num_layers * sizeof(__half))) != cudaSuccess) {
+      std::string m = std::string("f16 weights: ") + cudaGetErrorString(e);
+      wc_t5_destroy(h);
+      return fail(nullptr, WC_E_CUDA, m);
+    }
+    __half* hp = h->arena_f16;
+    auto deq = [&](const uint8_t* q4k, int64_t rows, int64_t K, __half*& dst) -> bool {
+      dst = hp;
+      hp += rows * K;
+      return q4k_dequant_f16_launch(q4k, rows * K / 256, dst, h->stream) == cudaSuccess;
+    };
+    for (int l = 0; l < cfg.num_layers && ok; ++l) {
+      LayerW& w = h->layers[l];
+      ok = deq(w.qkv, 3 * I, D, w.h_qkv) && deq(w.o, D, I, w.h_o) && deq(w.wi0, F, D, w.h_wi0) &&
+           deq(w.wi1, F, D, w.h_wi1) && deq(w.wo, D, F, w.h_wo) &&
+           make_act_map(&w.tmh_qkv, w.h_qkv, 3 * I, D, kGemm2WBoxRows) &&
+           make_act_map(&w.tmh_o, w.h_o, D, I, kGemm2WBoxRows) &&
+           make_act_map(&w.tmh_wi0, w.h_wi0, F, D, kGemm2WBoxRows) &&
+           make_act_map(&w.tmh_wi1, w.h_wi1, F, D, kGemm2WBoxRows) &&
+           make_act_map(&w.tmh_wo, w.h_wo, D, F, kGemm2WBoxRows);
+    }
+    if (ok) ok = cudaStreamSynchronize(h->stream) == cudaSuccess;
+    if (!ok) {
+      wc_t5_destroy(h);
+      return fail(nullptr, WC_E_CUDA, "dequantising the f16 layer weights failed");
+    }
   }
   *out = h;
   return WC_OK;
@@ -715,10 +748,46 @@ uint32_t* kernel_status_word() {
 }
 }  // namespace
 
+extern "C" int wc_q4k_dequant_f16(const void* d_blocks, int64_t nblocks, void* d_out_f16, void* stream) {
+  if (nblocks < 0 || (nblocks > 0 && (!d_blocks || !d_out_f16))) return WC_E_INVALID_ARG;
+  return q4k_dequant_f16_launch(static_cast<const uint8_t*>(d_blocks), nblocks, static_cast<__half*>(d_out_f16),
+                                static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? WC_OK
+             : WC_E_CUDA;
+}
+
 extern "C" int wc_q4k_dequant(const void* d_blocks, int64_t nblocks, float* d_out, void* stream) {
   if (nblocks < 0 || (nblocks > 0 && (!d_blocks || !d_out))) return WC_E_INVALID_ARG;
   return q4k_dequant_launch(static_cast<const uint8_t*>(d_blocks), nblocks, d_out,
                             static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? WC_OK
+             : WC_E_CUDA;
+}
+
+extern "C" int wc_gemm_f16(const void* d_x, int M, int K, const void* d_w, const void* d_w_up, int N, int epilogue,
+                           void* d_out, void* stream) {
+  if (!d_x || !d_w || !d_out || M < 1 || K < 256 || K % 256 || N < 128 || N % 128) return WC_E_INVALID_ARG;
+  if (epilogue < 0 || epilogue > 3) return WC_E_INVALID_ARG;
+  if (epilogue == kEpiGeGLU && !d_w_up) return WC_E_INVALID_ARG;
+  const int tile_n = epilogue == kEpiGeGLU ? 2 * N : N;
+  if (!gemm2_q4k_supports(epilogue, M, tile_n, K)) return WC_E_UNSUPPORTED;
+  CUtensorMap ta, tw0, tw1, tout;
+  if (!make_act_map(&ta, d_x, M, K) || !make_act_map(&tw0, d_w, N, K, kGemm2WBoxRows) ||
+      !make_act_map(&tw1, epilogue == kEpiGeGLU ? d_w_up : d_w, N, K, kGemm2WBoxRows) ||
+      !make_out_map(&tout, d_out, M, N, epilogue == kEpiF32 || epilogue == kEpiResid))
+    return WC_E_CUDA;
+  GemmParams p{};
+  p.M = M;
+  p.N = tile_n;
+  p.K = K;
+  p.out = d_out;
+  p.ldo = N;
+  p.status = kernel_status_word();
+  if (!p.status) return WC_E_CUDA;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return gemm2_q4k_launch(epilogue, ta, tw0, tw1, tout, p, device_sm_count(dev), static_cast<cudaStream_t>(stream),
+                          true) == cudaSuccess
              ? WC_OK
              : WC_E_CUDA;
 }
@@ -875,13 +944,13 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tm2_qkv, w.tm2_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
+    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tmh_qkv, w.tmh_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
     if ((e = attention_tc_launch(tm_qkv, att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) != cudaSuccess)
       return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tm2_o, w.tm2_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tmh_o, w.tmh_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
     if ((e = rmsnorm_launch(x, res_delta, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
-    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tm2_wi0, w.tm2_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
-    if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tm2_wo, w.tm2_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo))) return rc;
+    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tmh_wi0, w.tmh_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tmh_wo, w.tmh_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo))) return rc;
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(x, res_delta, next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
   }
