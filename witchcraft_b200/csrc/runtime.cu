@@ -293,43 +293,14 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
   return gemm(h, epi, bn, a, w0, w1, M, N, K, out, ldo, st);
 }
 
+int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half* hbuf, const CUtensorMap& tm_xn,
+               const CUtensorMap& tm_att, const CUtensorMap& tm_h, const uint32_t* ids, const int32_t* lengths,
+               int B, int L, float* out, float* norms, float* outn, cudaStream_t st);
+
 int forward_device(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, int L, float* out, float* norms,
                    float* outn, cudaStream_t st) {
-  const T5Config& c = h->cfg;
-  const int D = c.d_model, F = c.d_ff, I = h->inner, H = c.num_heads;
-  const int M = B * L;
-  CUtensorMap tm_qkv;
-  if (!make_act_map(&tm_qkv, h->qkv, M, 3 * I, 64)) return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for qkv");
-  // Residual adds: for large M the O / wo GEMM epilogue adds into x itself
-  // (TMA load-add-store) and the RMSNorm only normalises; otherwise the GEMM
-  // writes f32 into the dead qkv buffer and the RMSNorm adds it.
-  const bool fused_res = M >= kGemm2MinRows;
-  const int res_epi = fused_res ? kEpiResid : kEpiF32;
-  void* res_out = fused_res ? static_cast<void*>(h->x) : static_cast<void*>(h->qkv);
-  const float* res_delta = fused_res ? nullptr : reinterpret_cast<const float*>(h->qkv);
-  cudaError_t e;
-  if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, h->x, h->xn, st)) !=
-      cudaSuccess)
-    return cuda_fail(h, e, "embedding launch");
-  int rc;
-  for (int l = 0; l < c.num_layers; ++l) {
-    LayerW& w = h->layers[l];
-    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, h->tm_xn, w.tm_qkv, w.tm_qkv, w.tmh_qkv, w.tmh_qkv, M, 3 * I, D, h->qkv, 3 * I, st, h->xn, w.qkv, w.qkv)))
-      return rc;
-    if ((e = attention_tc_launch(tm_qkv, h->att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) !=
-        cudaSuccess)
-      return cuda_fail(h, e, "attention launch");
-    if ((rc = layer_gemm(h, res_epi, h->bn_o, h->tm_att, w.tm_o, w.tm_o, w.tmh_o, w.tmh_o, M, D, I, res_out, D, st, h->att, w.o, w.o))) return rc;
-    if ((e = rmsnorm_launch(h->x, res_delta, w.ln1, h->xn, M, D, c.eps, st)) != cudaSuccess)
-      return cuda_fail(h, e, "rmsnorm launch");
-    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, h->tm_xn, w.tm_wi0, w.tm_wi1, w.tmh_wi0, w.tmh_wi1, M, 2 * F, D, h->hbuf, F, st, h->xn, w.wi0, w.wi1))) return rc;
-    if ((rc = layer_gemm(h, res_epi, h->bn_wo, h->tm_h, w.tm_wo, w.tm_wo, w.tmh_wo, w.tmh_wo, M, D, F, res_out, D, st, h->hbuf, w.wo, w.wo))) return rc;
-    const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
-    if ((e = rmsnorm_launch(h->x, res_delta, next_ln, h->xn, M, D, c.eps, st)) != cudaSuccess)
-      return cuda_fail(h, e, "rmsnorm launch");
-  }
-  return gemm(h, kEpiProj, 128, h->tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
-              lengths, L);
+  return forward_on(h, h->x, h->xn, h->qkv, h->att, h->hbuf, h->tm_xn, h->tm_att, h->tm_h, ids, lengths, B, L, out,
+                    norms, outn, st);
 }
 
 int check_status(wc_t5* h, cudaStream_t st) {
@@ -923,8 +894,8 @@ uint8_t* noalloc_scratch_ptr(int dev, cudaError_t* err) {
   return ptrs[dev];
 }
 
-// The launch sequence of forward_device over caller-provided activation
-// buffers (x, xn, qkv, att, hbuf) and their tensor maps.
+// The launch sequence of one forward over the given activation buffers
+// (x, xn, qkv, att, hbuf) and their tensor maps.
 int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half* hbuf, const CUtensorMap& tm_xn,
                const CUtensorMap& tm_att, const CUtensorMap& tm_h, const uint32_t* ids, const int32_t* lengths,
                int B, int L, float* out, float* norms, float* outn, cudaStream_t st) {
@@ -933,7 +904,10 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   const int M = B * L;
   CUtensorMap tm_qkv;
   if (!make_act_map(&tm_qkv, qkv, M, 3 * I, 64)) return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for qkv");
-  const bool fused_res = M >= kGemm2MinRows;  // as in forward_device
+  // Residual adds: for large M the O / wo GEMM epilogue adds into x itself
+  // (TMA load-add-store) and the RMSNorm only normalises; otherwise the GEMM
+  // writes f32 into the dead qkv buffer and the RMSNorm adds it.
+  const bool fused_res = M >= kGemm2MinRows;
   const int res_epi = fused_res ? kEpiResid : kEpiF32;
   void* res_out = fused_res ? static_cast<void*>(x) : static_cast<void*>(qkv);
   const float* res_delta = fused_res ? nullptr : reinterpret_cast<const float*>(qkv);
