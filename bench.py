@@ -402,7 +402,54 @@ def kernel_measurements(enc, args, peak, peak_src):
     t = _time_launches(f, st, reps=20)
     afl = float(sum(12 * 4 * 64 * int(n) ** 2 for n in lens))
     micro["attention_config3"] = {"us": t * 1e6, "tflops": afl / t / 1e12, "frac_of_peak": afl / t / 1e12 / peak}
-    return roof, {"microbench": micro, "query_latency": query_latency(enc)}
+    return roof, {"microbench": micro, "query_latency": query_latency(enc), "codec": codec_measurement()}
+
+
+def codec_measurement(n_docs: int = 2048, cpu_docs: int = 256):
+    """embeddings_to_packed (src/packops.rs:172-301) of config-4-length
+    documents (L2-normalised synthetic rows): the GPU codec on n_docs, timed
+    with CUDA events around the device entry point (inputs resident), and the
+    C oracle on the first cpu_docs of them on one host core."""
+    import torch
+    from oracle import oracle as O
+    from witchcraft_b200._lib import check, lib
+    from witchcraft_b200.shard import config4_lengths
+    l = lib()
+    lens = config4_lengths(n_docs, seed=7)
+    rng = np.random.default_rng(8)
+    emb = rng.standard_normal((int(lens.sum()), 128)).astype(np.float32)
+    emb /= np.linalg.norm(emb, axis=1, keepdims=True)
+    rows = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    d_emb = torch.from_numpy(emb).cuda()
+    cap = l.wc_packed_bound(rows.ctypes.data, n_docs, 128)
+    d_out = torch.empty(cap, dtype=torch.uint8, device="cuda")
+    offs = np.empty(n_docs + 1, np.int64)
+    st = torch.cuda.Stream()
+    sp = ctypes.c_void_p(st.cuda_stream)
+
+    def run():
+        rc = l.wc_pack_embeddings_device(ctypes.c_void_p(d_emb.data_ptr()), rows.ctypes.data, n_docs, 128,
+                                         ctypes.c_void_p(d_out.data_ptr()), cap, offs.ctypes.data, sp)
+        if rc != 0:
+            raise RuntimeError(l.wc_codec_last_error())
+    run()
+    times = []
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        run()
+        b.record(st)
+        b.synchronize()
+        times.append(a.elapsed_time(b) / 1e3)
+    t = min(times)
+    n_cpu = int(rows[cpu_docs])
+    t0 = time.perf_counter()
+    for i in range(cpu_docs):
+        O.pack_embeddings(emb[rows[i]:rows[i + 1]])
+    tc = time.perf_counter() - t0
+    return {"what": "embeddings_to_packed, config-4 document lengths", "docs": n_docs, "rows": int(rows[-1]),
+            "gpu_rows_per_s": rows[-1] / t, "gpu_ms": t * 1e3, "bytes_per_row": offs[-1] / rows[-1],
+            "cpu_oracle_rows_per_s_1core": n_cpu / tc, "cpu_sample_docs": cpu_docs}
 
 
 def query_latency(enc, runs: int = 200):

@@ -23,7 +23,8 @@ _fp = ctypes.POINTER(ctypes.c_float)
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "oracle.c")):
+        srcs = [os.path.join(HERE, f) for f in ("oracle.c", "codec.c", "Makefile")]
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
             subprocess.run(["make", "-C", HERE, "CC=gcc"], check=True, capture_output=True)
         l = ctypes.CDLL(LIB_PATH)
         l.oracle_q4k_dequant.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
@@ -34,6 +35,12 @@ def lib():
         l.oracle_t5_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_void_p]
         l.oracle_gemm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3
+        l.oracle_pack.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64]
+        l.oracle_pack.restype = ctypes.c_int64
+        l.oracle_unpack.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64]
+        l.oracle_unpack.restype = ctypes.c_int64
+        l.oracle_packed_bound.argtypes = [ctypes.c_int64, ctypes.c_int]
+        l.oracle_packed_bound.restype = ctypes.c_int64
         l.oracle_num_threads.restype = ctypes.c_int
         l.oracle_set_threads.argtypes = [ctypes.c_int]
         _lib = l
@@ -151,3 +158,26 @@ class OracleEncoder:
         out = np.empty((B, L, self.cfg.d_proj), np.float32)
         lib().oracle_t5_encode(ctypes.addressof(self.w), _ptr(ids), _ptr(lens), B, L, _ptr(out))
         return out
+
+
+def pack_embeddings(emb: np.ndarray) -> bytes:
+    """embeddings_to_packed (src/packops.rs:172-301) of one [rows, cols] f32 matrix."""
+    emb = np.ascontiguousarray(emb, np.float32)
+    rows, cols = emb.shape
+    cap = lib().oracle_packed_bound(rows, cols)
+    out = np.empty(cap, np.uint8)
+    n = lib().oracle_pack(emb.ctypes.data, rows, cols, out.ctypes.data, cap)
+    if n < 0:
+        raise ValueError("embeddings_to_packed failed")
+    return out[:n].tobytes()
+
+
+def unpack_embeddings(buf: bytes, cols: int = 128) -> np.ndarray:
+    """embeddings_from_packed (src/packops.rs:303-438) -> [rows, cols] f32, L2-normalised."""
+    b = np.frombuffer(buf, np.uint8)
+    rows = int(b[:4].view(np.uint32)[0]) if len(b) >= 4 else 0
+    out = np.empty(max(rows, 1) * cols, np.float32)
+    n = lib().oracle_unpack(b.ctypes.data, len(b), cols, out.ctypes.data, out.size)
+    if n < 0:
+        raise ValueError("malformed packed embeddings")
+    return out[: n * cols].reshape(n, cols)

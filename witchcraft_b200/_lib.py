@@ -1,4 +1,4 @@
-"""ctypes binding of the native library (include/wc_t5cuda.h).
+"""ctypes binding of the native library (include/wc_t5cuda.h, include/wc_codec.h).
 
 The library is built in-tree by `witchcraft_b200.build`; loading fails loudly
 when it is missing.  There is no CPU fallback anywhere in this package.
@@ -11,7 +11,8 @@ import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libwc_t5cuda.so")
-HEADER = os.path.join(os.path.dirname(HERE), "include", "wc_t5cuda.h")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+HEADER = os.path.join(INCLUDE, "wc_t5cuda.h")
 
 WC_OK = 0
 ERRORS = {-1: "WC_E_INVALID_ARG", -2: "WC_E_GGUF", -3: "WC_E_UNSUPPORTED", -4: "WC_E_CUDA",
@@ -41,6 +42,13 @@ _SIGNATURES = {
     "wc_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "wc_t5_relative_bucket": (c_int, [c_int, c_int, c_int, c_int]),
     "wc_selftest_wait_timeout": (c_int, [ctypes.c_uint64]),
+    "wc_packed_bound": (c_int64, [c_void_p, c_int, c_int]),
+    "wc_pack_embeddings_device": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
+    "wc_pack_embeddings": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p, c_int]),
+    "wc_unpack_embeddings_device": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p,
+                                            c_void_p]),
+    "wc_unpack_embeddings": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p, c_int]),
+    "wc_codec_last_error": (ctypes.c_char_p, []),
 }
 
 
@@ -65,9 +73,12 @@ def lib() -> ctypes.CDLL:
 
 
 def header_symbols() -> list[str]:
-    """Function names declared in include/wc_t5cuda.h."""
-    txt = open(HEADER).read()
-    return sorted(set(re.findall(r"\b(wc_[a-z0-9_]+)\s*\(", txt)))
+    """Function names declared in include/*.h."""
+    names = set()
+    for f in sorted(os.listdir(INCLUDE)):
+        if f.endswith(".h"):
+            names.update(re.findall(r"\b(wc_[a-z0-9_]+)\s*\(", open(os.path.join(INCLUDE, f)).read()))
+    return sorted(names)
 
 
 def check(code: int, handle=None) -> None:

@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libwc_t5cuda.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 
-CUDA_SOURCES = ["gemm_q4k.cu", "gemm2_q4k.cu", "gemv_q4k.cu", "attention_tc.cu", "elementwise.cu", "runtime.cu"]
+CUDA_SOURCES = ["gemm_q4k.cu", "gemm2_q4k.cu", "gemv_q4k.cu", "attention_tc.cu", "elementwise.cu", "runtime.cu", "codec.cu"]
 CXX_SOURCES = ["t5_host.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -50,7 +50,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
     nvcc = _nvcc()
     os.makedirs(BUILD_DIR, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
-    headers.append(os.path.join(os.path.dirname(HERE), "include", "wc_t5cuda.h"))
+    inc = os.path.join(os.path.dirname(HERE), "include")
+    headers += [os.path.join(inc, f) for f in os.listdir(inc) if f.endswith(".h")]
     objs = []
     for src in CUDA_SOURCES:
         s = os.path.join(CSRC, src)
