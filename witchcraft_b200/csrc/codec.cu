@@ -19,11 +19,10 @@
 //                    remainder step ranks the remainders in parallel, a
 //                    stable descending order), and the rANS encoder table;
 //                    symbols are rewritten as indices into that table.
-//                    Then one thread of the CTA runs the window's rANS64
-//                    encode (src/rans64.rs:88-166), serial by construction,
-//                    from a table of the m symbols' encoder constants in
-//                    shared memory; the grid's CTAs encode windows in
-//                    parallel.
+//   pack_encode      one thread per window: the rANS64 encode
+//                    (src/rans64.rs:88-166), serial by construction, from the
+//                    window's table of encoder constants; all windows of a
+//                    chunk encode at once.
 //   pack_assemble    one CTA per window copies header and stream into place.
 // Decode mirrors it: unpack_decode (one CTA per window: the cumulative-
 // frequency tables in shared memory, one thread runs the serial rANS decode)
@@ -159,13 +158,12 @@ __device__ void warp_haar_inverse(float* x, float* tmp, int n0, int lane) {
 }
 
 // Shared memory of pack_transform / unpack_inverse: a union of the Haar
-// buffers (per warp: 2 x kWinRows floats), the histogram-scaling arrays
-// (remainders u64, counts, frequencies) and, after them, the frequency copy
-// plus the encoder table (16 KB + 64 KB).
+// buffers (per warp: 2 x kWinRows floats) and the histogram-scaling arrays
+// (remainders u64, counts, frequencies).
 constexpr int kHaarFloats = kWarps * 2 * kWinRows;
 constexpr size_t kTransformSmem =
-    std::max<size_t>(std::max<size_t>(kHaarFloats * sizeof(float), kMaxSyms * (sizeof(uint64_t) + 2 * sizeof(uint32_t))),
-                     kMaxSyms * sizeof(uint32_t) + kMaxSyms * 16);
+    std::max<size_t>(kHaarFloats * sizeof(float), kMaxSyms * (sizeof(uint64_t) + 2 * sizeof(uint32_t)));
+constexpr int kChunkWins = 4096;  // windows per transform + encode round (encoder tables: 64 KB each)
 
 __device__ __forceinline__ float block_max(float v, float* red) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
@@ -214,9 +212,9 @@ constexpr int kPairsOff = 256;
 constexpr size_t kHdrStride = kPairsOff + 4 * kMaxSyms;
 
 __global__ void __launch_bounds__(kThreads)
-    pack_transform(const float* __restrict__ emb, int cols, const WinDesc* __restrict__ wins, int n_wins,
-                   float* __restrict__ S, uint16_t* __restrict__ Q, uint32_t* __restrict__ hist_pool,
-                   uint8_t* __restrict__ hdr, uint8_t* __restrict__ enc, WinOut* __restrict__ wout,
+    pack_transform(const float* __restrict__ emb, int cols, const WinDesc* __restrict__ wins, int w_begin,
+                   int w_end, float* __restrict__ S, uint16_t* __restrict__ Q, uint32_t* __restrict__ hist_pool,
+                   uint8_t* __restrict__ hdr, EncSym* __restrict__ esyms, WinOut* __restrict__ wout,
                    uint32_t* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float s_sum[kMaxCols + 1];
@@ -228,7 +226,7 @@ __global__ void __launch_bounds__(kThreads)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* hist = hist_pool + static_cast<size_t>(blockIdx.x) * 65536;
 
-  for (int w = blockIdx.x; w < n_wins; w += gridDim.x) {
+  for (int w = w_begin + blockIdx.x; w < w_end; w += gridDim.x) {
     const WinDesc wd = wins[w];
     const int R = wd.rows;
     const float* E = emb + wd.row0 * cols;
@@ -388,16 +386,11 @@ __global__ void __launch_bounds__(kThreads)
     }
     __syncthreads();
     // -------- frequencies into the header, cumulative starts, encoder table
-    // (in the shared memory of cnt / freq, which are consumed here)
-    __syncthreads();
-    uint32_t* fcopy = reinterpret_cast<uint32_t*>(smem);  // rem is no longer needed
-    for (int i = tid; i < m; i += kThreads) fcopy[i] = freq[i];
-    __syncthreads();
-    EncSym* es = reinterpret_cast<EncSym*>(smem + kMaxSyms * sizeof(uint32_t));
+    EncSym* es = esyms + static_cast<size_t>(w - w_begin) * kMaxSyms;
     int cbase = 0;
     for (int i0 = 0; i0 < m; i0 += kThreads) {
       const int i = i0 + tid;
-      const int f = i < m ? static_cast<int>(fcopy[i]) : 0;
+      const int f = i < m ? static_cast<int>(freq[i]) : 0;
       int cum;
       const int tot = block_scan(f, s_redi, &cum);
       if (i < m) {
@@ -406,47 +399,57 @@ __global__ void __launch_bounds__(kThreads)
       }
       cbase += tot;
     }
-    // -------- symbols -> table indices, then the serial encode by thread 0
+    // -------- symbols -> table indices for the encoder
     for (int i = tid; i < n; i += kThreads) Qw[i] = static_cast<uint16_t>(hist[Qw[i]]);
-    __syncthreads();
-    if (tid == 0) {
-      uint8_t* buf = enc + 2 * wd.row0 * cols;
-      const int64_t cap = 2 * static_cast<int64_t>(n);
-      int64_t idx = cap;
-      uint64_t x = kRansL;
-      bool ok = true;
-      for (int k = 0; k < n && ok; ++k) {
-        const EncSym e = es[Qw[k]];
-        const uint64_t x_max = static_cast<uint64_t>(e.freq) << 51;  // ((2^31 >> 12) << 32) * freq
-        while (x >= x_max) {
-          if (idx < 4) {
-            ok = false;
-            break;
-          }
-          idx -= 4;
-          const uint32_t v = static_cast<uint32_t>(x);
-          buf[idx] = static_cast<uint8_t>(v);
-          buf[idx + 1] = static_cast<uint8_t>(v >> 8);
-          buf[idx + 2] = static_cast<uint8_t>(v >> 16);
-          buf[idx + 3] = static_cast<uint8_t>(v >> 24);
-          x >>= 32;
-        }
-        const uint64_t qq = __umul64hi(x, e.rcp_freq) >> e.rcp_shift;
-        x = x + e.bias + qq * ((1u << kRansBits) - e.freq);
-      }
-      if (ok && idx >= 8) {
-        idx -= 8;
-        for (int i = 0; i < 8; ++i) buf[idx + i] = static_cast<uint8_t>(x >> (8 * i));
-        wout[w].m = m;
-        wout[w].enc_start = static_cast<int>(idx);
-        wout[w].enc_len = static_cast<int>(cap - idx);
-      } else {
-        atomicOr(status, kErrEncodeOverflow);
-        wout[w].m = -1;
-      }
-    }
+    if (tid == 0) wout[w].m = m;
     __syncthreads();
   }
+}
+
+// One thread per window of [w_begin, w_end): rANS64 encode of its n symbols
+// in order into enc[2 row0 cols, + 2 n) from the back (src/rans64.rs:88-166).
+__global__ void pack_encode(int cols, const WinDesc* __restrict__ wins, int w_begin, int w_end,
+                            const uint16_t* __restrict__ Q, const EncSym* __restrict__ esyms,
+                            uint8_t* __restrict__ enc, WinOut* __restrict__ wout, uint32_t* __restrict__ status) {
+  const int w = w_begin + static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (w >= w_end || wout[w].m < 0) return;
+  const WinDesc wd = wins[w];
+  const int64_t n = static_cast<int64_t>(wd.rows) * cols;
+  const uint16_t* q = Q + wd.row0 * cols;
+  const EncSym* es = esyms + static_cast<size_t>(w - w_begin) * kMaxSyms;
+  uint8_t* buf = enc + 2 * wd.row0 * cols;
+  const int64_t cap = 2 * n;
+  int64_t idx = cap;
+  uint64_t x = kRansL;
+  for (int64_t k = 0; k < n; ++k) {
+    const EncSym e = es[q[k]];
+    const uint64_t x_max = static_cast<uint64_t>(e.freq) << 51;  // ((2^31 >> 12) << 32) * freq
+    while (x >= x_max) {
+      if (idx < 4) {
+        atomicOr(status, kErrEncodeOverflow);
+        wout[w].m = -1;
+        return;
+      }
+      idx -= 4;
+      const uint32_t v = static_cast<uint32_t>(x);
+      buf[idx] = static_cast<uint8_t>(v);
+      buf[idx + 1] = static_cast<uint8_t>(v >> 8);
+      buf[idx + 2] = static_cast<uint8_t>(v >> 16);
+      buf[idx + 3] = static_cast<uint8_t>(v >> 24);
+      x >>= 32;
+    }
+    const uint64_t qq = __umul64hi(x, e.rcp_freq) >> e.rcp_shift;
+    x = x + e.bias + qq * ((1u << kRansBits) - e.freq);
+  }
+  if (idx < 8) {
+    atomicOr(status, kErrEncodeOverflow);
+    wout[w].m = -1;
+    return;
+  }
+  idx -= 8;
+  for (int i = 0; i < 8; ++i) buf[idx + i] = static_cast<uint8_t>(x >> (8 * i));
+  wout[w].enc_start = static_cast<int>(idx);
+  wout[w].enc_len = static_cast<int>(cap - idx);
 }
 
 // One CTA per window: header and rANS bytes into the output stream at
@@ -714,17 +717,19 @@ extern "C" int wc_pack_embeddings_device(const float* d_emb, const int64_t* doc_
   Scratch& sc = g_scratch[dev];
   std::lock_guard<std::mutex> lk(sc.mu);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = std::min(n_wins, 2 * device_sms(dev));
+  const int grid = std::min(std::min(n_wins, kChunkWins), 3 * device_sms(dev));
+  const int chunk = std::min(n_wins, kChunkWins);
   float* S;
   uint16_t* Q;
   uint32_t* hist;
   uint8_t *hdr, *enc;
+  EncSym* es;
   WinOut* wout;
   WinDesc* dwins;
   int64_t *dwoff, *ddoc;
   if (grow(sc, 0, static_cast<size_t>(total_rows) * cols, &S) || grow(sc, 1, static_cast<size_t>(total_rows) * cols, &Q) ||
       grow(sc, 2, static_cast<size_t>(grid) * 65536, &hist) || grow(sc, 3, static_cast<size_t>(n_wins) * kHdrStride, &hdr) ||
-      grow(sc, 4, static_cast<size_t>(2 * total_rows * cols), &enc) ||
+      grow(sc, 4, static_cast<size_t>(2 * total_rows * cols), &enc) || grow(sc, 5, static_cast<size_t>(chunk) * kMaxSyms, &es) ||
       grow(sc, 6, static_cast<size_t>(n_wins) + 1, &wout) || grow(sc, 7, static_cast<size_t>(n_wins), &dwins) ||
       grow(sc, 8, static_cast<size_t>(n_wins) + 1, &dwoff) || grow(sc, 9, static_cast<size_t>(n_docs) + 2, &ddoc))
     return codec_fail(WC_E_CUDA, "codec scratch allocation failed");
@@ -743,7 +748,12 @@ extern "C" int wc_pack_embeddings_device(const float* d_emb, const int64_t* doc_
       (e = cudaMemcpyAsync(ddoc, doc_rows, sizeof(int64_t) * (n_docs + 1), cudaMemcpyHostToDevice, st)) ||
       (e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st)))
     return codec_fail(WC_E_CUDA, std::string("codec setup copies: ") + cudaGetErrorString(e));
-  pack_transform<<<grid, kThreads, kTransformSmem, st>>>(d_emb, cols, dwins, n_wins, S, Q, hist, hdr, enc, wout, status);
+  for (int w0 = 0; w0 < n_wins; w0 += kChunkWins) {
+    const int w1 = std::min(n_wins, w0 + kChunkWins);
+    pack_transform<<<std::min(grid, w1 - w0), kThreads, kTransformSmem, st>>>(d_emb, cols, dwins, w0, w1, S, Q, hist,
+                                                                                hdr, es, wout, status);
+    pack_encode<<<(w1 - w0 + 31) / 32, 32, 0, st>>>(cols, dwins, w0, w1, Q, es, enc, wout, status);
+  }
   if ((e = cudaGetLastError()) != cudaSuccess)
     return codec_fail(WC_E_CUDA, std::string("codec launch: ") + cudaGetErrorString(e));
   std::vector<WinOut> wo(n_wins + 1);
