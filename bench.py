@@ -402,7 +402,46 @@ def kernel_measurements(enc, args, peak, peak_src):
     t = _time_launches(f, st, reps=20)
     afl = float(sum(12 * 4 * 64 * int(n) ** 2 for n in lens))
     micro["attention_config3"] = {"us": t * 1e6, "tflops": afl / t / 1e12, "frac_of_peak": afl / t / 1e12 / peak}
-    return roof, {"microbench": micro, "query_latency": query_latency(enc), "codec": codec_measurement()}
+    return roof, {"microbench": micro, "query_latency": query_latency(enc), "codec": codec_measurement(),
+                  "index_assign": assign_measurement()}
+
+
+def assign_measurement(m: int = 262144, cpu_rows: int = 256):
+    """matmul_argmax_batched (src/lib.rs:187-208) with the reference's center
+    count k = round(16 sqrt(m)): the GPU kernel (FP32 FMA chains on the CUDA
+    cores) timed with CUDA events, against the FP32 FMA peak
+    (148 SMs x 128 lanes x 2 FLOP x the SM clock), and the C oracle on
+    cpu_rows rows with all host threads."""
+    import torch
+    from oracle import oracle as O
+    from witchcraft_b200 import index as I
+    k = int(round(16 * m ** 0.5))
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((m, 128)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    c = x[rng.choice(m, k, replace=False)]
+    dx, dc = torch.from_numpy(x).cuda(), torch.from_numpy(c).cuda()
+    I.assign(dx, dc)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        I.assign(dx, dc)
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) / 1e3)
+    t = min(times)
+    flops = 2.0 * m * k * 128
+    import torch as _t
+    sm_mhz = _t.cuda.get_device_properties(0).clock_rate / 1e3 if hasattr(_t.cuda.get_device_properties(0), "clock_rate") else 1965.0
+    peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+    t0 = time.perf_counter()
+    O.assign_centers(x[:cpu_rows], c)
+    tc = time.perf_counter() - t0
+    return {"what": "nearest-center assignment, k = round(16 sqrt(m))", "m": m, "k": k, "gpu_ms": t * 1e3,
+            "gpu_tflops_fp32": flops / t / 1e12, "fp32_fma_peak_tflops": peak, "frac_of_fp32_peak": flops / t / 1e12 / peak,
+            "gpu_rows_per_s": m / t, "cpu_oracle_rows_per_s": cpu_rows / tc, "cpu_threads": O.lib().oracle_num_threads()}
 
 
 def codec_measurement(n_docs: int = 2048, cpu_docs: int = 256):

@@ -23,7 +23,7 @@ _fp = ctypes.POINTER(ctypes.c_float)
 def lib():
     global _lib
     if _lib is None:
-        srcs = [os.path.join(HERE, f) for f in ("oracle.c", "codec.c", "Makefile")]
+        srcs = [os.path.join(HERE, f) for f in ("oracle.c", "codec.c", "index.c", "Makefile")]
         if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
             subprocess.run(["make", "-C", HERE, "CC=gcc"], check=True, capture_output=True)
         l = ctypes.CDLL(LIB_PATH)
@@ -41,6 +41,12 @@ def lib():
         l.oracle_unpack.restype = ctypes.c_int64
         l.oracle_packed_bound.argtypes = [ctypes.c_int64, ctypes.c_int]
         l.oracle_packed_bound.restype = ctypes.c_int64
+        l.oracle_assign.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                    ctypes.c_void_p]
+        l.oracle_kmeans_update.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
+                                           ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        l.oracle_residual_q4.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p]
         l.oracle_num_threads.restype = ctypes.c_int
         l.oracle_set_threads.argtypes = [ctypes.c_int]
         _lib = l
@@ -181,3 +187,34 @@ def unpack_embeddings(buf: bytes, cols: int = 128) -> np.ndarray:
     if n < 0:
         raise ValueError("malformed packed embeddings")
     return out[: n * cols].reshape(n, cols)
+
+
+def assign_centers(x: np.ndarray, centers: np.ndarray) -> np.ndarray:
+    """matmul_argmax_batched (src/lib.rs:187-208): first argmax of x c^T per row."""
+    x = np.ascontiguousarray(x, np.float32)
+    c = np.ascontiguousarray(centers, np.float32)
+    out = np.empty(len(x), np.uint32)
+    lib().oracle_assign(x.ctypes.data, len(x), c.ctypes.data, len(c), x.shape[1], out.ctypes.data)
+    return out
+
+
+def kmeans_update(x: np.ndarray, idx: np.ndarray, k: int, empty_src: np.ndarray):
+    """One k-means update (src/lib.rs:238-274) -> (centers [k, dim], counts)."""
+    x = np.ascontiguousarray(x, np.float32)
+    idx = np.ascontiguousarray(idx, np.uint32)
+    es = np.ascontiguousarray(empty_src, np.int64)
+    out = np.empty((k, x.shape[1]), np.float32)
+    counts = np.empty(k, np.uint32)
+    lib().oracle_kmeans_update(x.ctypes.data, len(x), x.shape[1], idx.ctypes.data, k, es.ctypes.data,
+                               out.ctypes.data, counts.ctypes.data)
+    return out, counts
+
+
+def residual_q4(x: np.ndarray, idx: np.ndarray, centers: np.ndarray) -> np.ndarray:
+    """4-bit companded residual codes (src/lib.rs:1376) -> [m, dim / 2] bytes."""
+    x = np.ascontiguousarray(x, np.float32)
+    idx = np.ascontiguousarray(idx, np.uint32)
+    c = np.ascontiguousarray(centers, np.float32)
+    out = np.empty((len(x), x.shape[1] // 2), np.uint8)
+    lib().oracle_residual_q4(x.ctypes.data, len(x), x.shape[1], idx.ctypes.data, c.ctypes.data, out.ctypes.data)
+    return out

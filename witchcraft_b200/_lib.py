@@ -49,6 +49,11 @@ _SIGNATURES = {
                                             c_void_p]),
     "wc_unpack_embeddings": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p, c_int]),
     "wc_codec_last_error": (ctypes.c_char_p, []),
+    "wc_assign_centers": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "wc_kmeans_update": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                 c_void_p]),
+    "wc_residual_q4": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "wc_index_last_error": (ctypes.c_char_p, []),
 }
 
 
