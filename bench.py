@@ -403,7 +403,43 @@ def kernel_measurements(enc, args, peak, peak_src):
     afl = float(sum(12 * 4 * 64 * int(n) ** 2 for n in lens))
     micro["attention_config3"] = {"us": t * 1e6, "tflops": afl / t / 1e12, "frac_of_peak": afl / t / 1e12 / peak}
     return roof, {"microbench": micro, "query_latency": query_latency(enc), "codec": codec_measurement(),
-                  "index_assign": assign_measurement()}
+                  "index_assign": assign_measurement(), "query_scoring": query_scoring_measurement()}
+
+
+def query_scoring_measurement(rows: int = 200000, m: int = 32, per_sub: int = 8):
+    """match_centroids' candidate scoring (src/lib.rs:715-808) for one query of
+    m tokens over `rows` indexed candidates (4-bit residual codes, 1024
+    clusters, sub-chunks of per_sub rows, 4 sub-chunks per document): the GPU
+    scorer through its host entry (copies in and out included) and the C
+    oracle on one host core."""
+    import torch
+    from oracle import oracle as O
+    from witchcraft_b200 import query as Qm
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal((m, 128)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    n_cent = 1024
+    cs = (rng.standard_normal((m, n_cent)) * 0.2).astype(np.float32)
+    codes = rng.integers(0, 256, (rows, 64), dtype=np.uint8)
+    cluster = rng.integers(0, n_cent, rows).astype(np.uint32)
+    n_groups = rows // per_sub
+    c = Qm.Candidates(q=q, codes=codes, cluster=cluster, cscores=cs, raw=np.zeros((0, 128), np.float32),
+                      group_rows=np.arange(rows, dtype=np.int64),
+                      group_start=np.arange(0, rows + 1, per_sub, dtype=np.int64),
+                      doc_start=np.arange(0, n_groups + 1, 4, dtype=np.int64),
+                      group_keys=[(g // 4, g % 4) for g in range(n_groups)], missing=np.zeros(m, np.float32))
+    table = Qm.q4_table()
+    Qm.score_gpu(c, table)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(5):
+        Qm.score_gpu(c, table)
+    tg = (time.perf_counter() - t0) / 5
+    t0 = time.perf_counter()
+    O.score_candidates(q, codes, cluster, cs, table, c.raw, c.group_rows, c.group_start, c.doc_start, c.missing)
+    tc = time.perf_counter() - t0
+    return {"what": "candidate scoring of one query (m tokens x rows, 4-bit residuals)", "m": m, "rows": rows,
+            "gpu_ms_with_copies": tg * 1e3, "cpu_oracle_ms_1core": tc * 1e3}
 
 
 def assign_measurement(m: int = 262144, cpu_rows: int = 256):

@@ -23,7 +23,7 @@ _fp = ctypes.POINTER(ctypes.c_float)
 def lib():
     global _lib
     if _lib is None:
-        srcs = [os.path.join(HERE, f) for f in ("oracle.c", "codec.c", "index.c", "Makefile")]
+        srcs = [os.path.join(HERE, f) for f in ("oracle.c", "codec.c", "index.c", "query.c", "Makefile")]
         if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
             subprocess.run(["make", "-C", HERE, "CC=gcc"], check=True, capture_output=True)
         l = ctypes.CDLL(LIB_PATH)
@@ -47,6 +47,13 @@ def lib():
                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         l.oracle_residual_q4.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
                                          ctypes.c_void_p, ctypes.c_void_p]
+        l.oracle_q4_table.argtypes = [ctypes.c_void_p]
+        l.oracle_similarities.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                          ctypes.c_void_p]
+        l.oracle_score_candidates.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                              ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
         l.oracle_num_threads.restype = ctypes.c_int
         l.oracle_set_threads.argtypes = [ctypes.c_int]
         _lib = l
@@ -217,4 +224,38 @@ def residual_q4(x: np.ndarray, idx: np.ndarray, centers: np.ndarray) -> np.ndarr
     c = np.ascontiguousarray(centers, np.float32)
     out = np.empty((len(x), x.shape[1] // 2), np.uint8)
     lib().oracle_residual_q4(x.ctypes.data, len(x), x.shape[1], idx.ctypes.data, c.ctypes.data, out.ctypes.data)
+    return out
+
+
+def q4_table() -> np.ndarray:
+    """make_q4_dequant_table (src/packops.rs:14-24)."""
+    t = np.empty(16, np.float32)
+    lib().oracle_q4_table(t.ctypes.data)
+    return t
+
+
+def score_candidates(q, codes, cluster, cscores, table, raw, group_rows, group_start, doc_start, missing):
+    """match_centroids' sub-chunk scores over a prepared candidate set (src/lib.rs:715-808)."""
+    q = np.ascontiguousarray(q, np.float32)
+    m, dim = q.shape
+    codes = np.ascontiguousarray(codes, np.uint8).reshape(-1, dim // 2)
+    cluster = np.ascontiguousarray(cluster, np.uint32)
+    cscores = np.ascontiguousarray(cscores, np.float32)
+    raw = np.ascontiguousarray(raw, np.float32).reshape(-1, dim)
+    gr, gs, ds = (np.ascontiguousarray(a, np.int64) for a in (group_rows, group_start, doc_start))
+    miss = np.ascontiguousarray(missing, np.float32)
+    out = np.empty(len(gs) - 1, np.float32)
+    lib().oracle_score_candidates(q.ctypes.data, m, dim, codes.ctypes.data, cluster.ctypes.data, cscores.ctypes.data,
+                                  cscores.shape[1] if cscores.ndim == 2 else 1, np.ascontiguousarray(table, np.float32).ctypes.data,
+                                  len(codes), raw.ctypes.data, gr.ctypes.data, gs.ctypes.data, ds.ctypes.data,
+                                  len(ds) - 1, miss.ctypes.data, out.ctypes.data)
+    return out
+
+
+def similarities(q: np.ndarray, c: np.ndarray) -> np.ndarray:
+    """Query-centroid similarities (src/lib.rs:637-640) as fmaf chains."""
+    q = np.ascontiguousarray(q, np.float32)
+    c = np.ascontiguousarray(c, np.float32)
+    out = np.empty((len(q), len(c)), np.float32)
+    lib().oracle_similarities(q.ctypes.data, len(q), c.ctypes.data, len(c), q.shape[1], out.ctypes.data)
     return out

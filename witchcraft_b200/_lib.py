@@ -54,6 +54,11 @@ _SIGNATURES = {
                                  c_void_p]),
     "wc_residual_q4": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "wc_index_last_error": (ctypes.c_char_p, []),
+    "wc_score_candidates": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64,
+                                    c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "wc_q4_table": (c_int, [c_void_p]),
+    "wc_similarities": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "wc_query_last_error": (ctypes.c_char_p, []),
 }
 
 
