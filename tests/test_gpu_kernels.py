@@ -188,7 +188,10 @@ def _attention_torch(qkv, B, L, H, lengths, bias_tab):
 
 
 @pytest.mark.parametrize("B,L,lengths", [(2, 128, [128, 128]), (4, 200, [200, 130, 64, 1]),
-                                         (2, 65, [65, 33]), (1, 2048, [2048]), (3, 1, [1, 1, 1])])
+                                         (2, 65, [65, 33]), (1, 2048, [2048]), (3, 1, [1, 1, 1]),
+                                         # L <= 64: the mma.sync kernel of short batches
+                                         (4, 32, [32, 17, 1, 5]), (2, 64, [64, 40]), (3, 17, [17, 9, 16]),
+                                         (2, 2, [2, 1])])
 def test_attention_matches_oracle(B, L, lengths):
     H = 12
     g = torch.Generator().manual_seed(B * 1000 + L)

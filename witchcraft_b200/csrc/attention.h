@@ -22,4 +22,10 @@ struct BucketThresholds {
 cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const int32_t* lengths, int B, int L, int H,
                                 const float* bias_tab, const BucketThresholds& bt, uint32_t* status, cudaStream_t st);
 
+// Short padded batches (1 <= L <= 64, the query path): mma.sync kernel over
+// the raw QKV pointer, one CTA per (sequence, head).
+bool attention_small_supports(int L);
+cudaError_t attention_small_launch(const __half* qkv, __half* out, const int32_t* lengths, int B, int L, int H,
+                                   const float* bias_tab, const BucketThresholds& bt, cudaStream_t st);
+
 }  // namespace wc

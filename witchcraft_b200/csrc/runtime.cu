@@ -824,6 +824,11 @@ extern "C" int wc_attention(const void* d_qkv, int B, int L, int H, const int32_
       num_buckets < 2 || num_buckets > 64 || max_distance < 1)
     return WC_E_INVALID_ARG;
   const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
+  if (attention_small_supports(L))
+    return attention_small_launch(static_cast<const __half*>(d_qkv), static_cast<__half*>(d_out), d_lengths, B, L, H,
+                                  d_bias_table, bt, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? WC_OK
+               : WC_E_CUDA;
   CUtensorMap tm;
   if (!make_act_map(&tm, d_qkv, static_cast<uint64_t>(B) * L, 3 * H * 64, 64)) return WC_E_CUDA;
   uint32_t* status = kernel_status_word();
@@ -919,8 +924,10 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
     if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tmh_qkv, w.tmh_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
-    if ((e = attention_tc_launch(tm_qkv, att, lengths, B, L, H, h->rel_bias, h->bt, h->d_status, st)) != cudaSuccess)
-      return cuda_fail(h, e, "attention launch");
+    e = attention_small_supports(L) ? attention_small_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)
+                                    : attention_tc_launch(tm_qkv, att, lengths, B, L, H, h->rel_bias, h->bt,
+                                                          h->d_status, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "attention launch");
     if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tmh_o, w.tmh_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
     if ((e = rmsnorm_launch(x, res_delta, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
     if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tmh_wi0, w.tmh_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
