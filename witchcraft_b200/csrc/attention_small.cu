@@ -50,6 +50,11 @@ __device__ __forceinline__ float ex2s(float x) {
   return y;
 }
 
+__device__ __forceinline__ void cp16s(uint32_t dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0)
+               : "memory");
+}
+
 __device__ __forceinline__ int bucket_of(const BucketThresholds& bt, int delta) {
   const int d = delta < 0 ? -delta : delta;
   int f = 0;
@@ -65,6 +70,7 @@ __global__ void __launch_bounds__(128)
   __shared__ __align__(16) uint8_t sK[kL * kRowB];
   __shared__ __align__(16) uint8_t sV[kL * kRowB];
   __shared__ float sBias[2 * kL];  // bias(key - query = delta) at delta + kL - 1, * log2(e)
+  __shared__ float sCol[64];       // this head's column of the bias table
   pdl_wait();
   pdl_launch_next();
   const int h = blockIdx.x, b = blockIdx.y;
@@ -79,15 +85,19 @@ __global__ void __launch_bounds__(128)
     }
     return;
   }
-  for (int i = tid; i < 3 * kL * 8; i += 128) {
+  // all loads in flight at once: Q, K, V rows (past L zero-filled) by cp.async
+#pragma unroll
+  for (int k = 0; k < 3 * kL * 8 / 128; ++k) {
+    const int i = tid + 128 * k;
     const int mat = i / (kL * 8), rem = i % (kL * 8), r = rem >> 3, c = rem & 7;
-    uint8_t* dst = (mat == 0 ? sQ : mat == 1 ? sK : sV) + r * kRowB + c * 16;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < L) v = *reinterpret_cast<const uint4*>(qkv + (row0 + r) * (3 * inner) + mat * inner + h * kDh + c * 8);
-    *reinterpret_cast<uint4*>(dst) = v;
+    const uint32_t dst = smem_u32(mat == 0 ? sQ : mat == 1 ? sK : sV) + r * kRowB + c * 16;
+    cp16s(dst, qkv + (row0 + (r < L ? r : 0)) * (3 * inner) + mat * inner + h * kDh + c * 8, r < L);
   }
-  for (int i = tid; i < 2 * kL - 1; i += 128)
-    sBias[i] = bias_tab[bucket_of(bt, i - (kL - 1)) * H + h] * 1.4426950408889634f;
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (tid < 2 * bt.half) sCol[tid] = bias_tab[tid * H + h] * 1.4426950408889634f;
+  __syncthreads();
+  for (int i = tid; i < 2 * kL - 1; i += 128) sBias[i] = sCol[bucket_of(bt, i - (kL - 1))];
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   const int q0 = warp * 16;
   if (q0 >= L) return;

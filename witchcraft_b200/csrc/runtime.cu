@@ -817,13 +817,32 @@ extern "C" int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const
              : WC_E_CUDA;
 }
 
+namespace wc {
+namespace {
+// Thresholds of the last (num_buckets, max_distance) asked for: computing
+// them takes thousands of reference bucket evaluations on the host.
+BucketThresholds cached_thresholds(int num_buckets, int max_distance) {
+  static std::mutex mu;
+  static int key[2] = {-1, -1};
+  static BucketThresholds bt{};
+  std::lock_guard<std::mutex> lk(mu);
+  if (key[0] != num_buckets || key[1] != max_distance) {
+    bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
+    key[0] = num_buckets;
+    key[1] = max_distance;
+  }
+  return bt;
+}
+}  // namespace
+}  // namespace wc
+
 extern "C" int wc_attention(const void* d_qkv, int B, int L, int H, const int32_t* d_lengths,
                             const float* d_bias_table, int num_buckets, int max_distance, void* d_out,
                             void* stream) {
   if (!d_qkv || !d_lengths || !d_bias_table || !d_out || B < 1 || L < 1 || L > kMaxL || H < 1 ||
       num_buckets < 2 || num_buckets > 64 || max_distance < 1)
     return WC_E_INVALID_ARG;
-  const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
+  const BucketThresholds bt = cached_thresholds(num_buckets, max_distance);
   if (attention_small_supports(L))
     return attention_small_launch(static_cast<const __half*>(d_qkv), static_cast<__half*>(d_out), d_lengths, B, L, H,
                                   d_bias_table, bt, static_cast<cudaStream_t>(stream)) == cudaSuccess
@@ -843,7 +862,7 @@ extern "C" int wc_t5_relative_bucket(int query, int key, int num_buckets, int ma
   if (num_buckets < 2 || num_buckets > 64 || max_distance < 1 || query < 0 || key < 0 || query >= kMaxL ||
       key >= kMaxL)
     return WC_E_INVALID_ARG;
-  const BucketThresholds bt = t5_bucket_thresholds(num_buckets, max_distance, kMaxL);
+  const BucketThresholds bt = cached_thresholds(num_buckets, max_distance);
   return t5_bucket_from_thresholds(bt, key - query);
 }
 
