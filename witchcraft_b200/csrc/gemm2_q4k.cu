@@ -23,7 +23,7 @@
 //   warp 1      TMEM allocation; MMA issue (even CTA, one thread)
 //   warps 2-9   dequant: raw Q4_K -> f16 K-major 128-B-swizzled B stages
 //   warps 10-13 epilogue: tcgen05.ld -> registers -> swizzled smem staging ->
-//               TMA tensor store (kEpiResid: TMA load of the x tile, add, TMA store)
+//               TMA tensor store (kEpiResid: TMA reduce-add into x)
 // With WF16 the weights are already f16 ([N][K], dequantised once from the
 // same Q4_K bytes with the same arithmetic, so the operands are bit-identical):
 // the producer TMA-loads each CTA's 128-row B half into the stage of its X
@@ -193,8 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty_b = full_b + kSB;        // [kSB]  each CTA: MMA done with the stage
   uint64_t* acc_full = empty_b + kSB;      // [2]    each CTA: accumulator ready
   uint64_t* acc_empty = acc_full + 2;      // [2]    even CTA: 16 epilogue warps drained it
-  uint64_t* xload_bars = acc_empty + 2;    // [4 epilogue warps][2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xload_bars + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -225,7 +224,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 2 * kEpiWarps);
     }
-    for (int i = 0; i < 8; ++i) mbar_init(&xload_bars[i], 1);
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW0);
@@ -354,8 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
     uint8_t* sOutW = smem + kOffOut + (warp - 10) * 2 * kOutBytes;
-    uint64_t* xload = xload_bars + (warp - 10) * 2;  // kEpiResid: x tile landed in staging buffer 0 / 1
-    uint32_t ostage = 0, xphase = 0;
+    uint32_t ostage = 0;
     const uint32_t acc_empty_leader0 = map_to_rank(&acc_empty[0], 0);
     uint32_t it = 0;
     for (int tile = cid; tile < n_total; tile += ncl, ++it) {
@@ -366,63 +363,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + row;
       const int nt = tile % n_tiles;
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
-      if (EPI == kEpiResid) {
-        // x += acc through TMA: each 32-row x 32-column f32 tile of x is
-        // loaded into this warp's staging buffer (the next one is prefetched
-        // while the current one is updated), the accumulator is added in
-        // shared memory and the tile is stored back; rows past M are
-        // zero-filled on load and clipped on store.
-        const int col_base = nt * kBN;
-        const int y0 = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + q * 32;
-        auto issue_load = [&](int ci) {
-          const uint32_t stg = (ostage + ci) & 1;
-          if (lane == 0) {
-            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // its last store has read it
-            mbar_arrive_expect_tx(&xload[stg], kOutBytes);
-            tma_load_2d(sOutW + stg * kOutBytes, &tmOut, &xload[stg], col_base + 32 * ci, y0);
-          }
-        };
-        issue_load(0);
-#pragma unroll 1
-        for (int ci = 0; ci < kBN / 32; ++ci) {
-          const uint32_t stg = (ostage + ci) & 1;
-          float v[32];
-          tmem_ld_32x32b_x32(tb + 32 * ci, v);
-          __syncwarp();
-          if (ci + 1 < kBN / 32) issue_load(ci + 1);
-          const bool ld_ok = mbar_wait(&xload[stg], (xphase >> stg) & 1, p.status);
-          xphase ^= 1u << stg;
-          uint8_t* srow = sOutW + stg * kOutBytes + lane * 128;
-          if (ld_ok) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              float4* cell = reinterpret_cast<float4*>(srow + ((k ^ (lane & 7)) << 4));
-              float4 x = *cell;
-              x.x += v[4 * k];
-              x.y += v[4 * k + 1];
-              x.z += v[4 * k + 2];
-              x.w += v[4 * k + 3];
-              *cell = x;
-            }
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            asm volatile(
-                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                    reinterpret_cast<uint64_t>(&tmOut)),
-                "r"(smem_u32(srow - lane * 128)), "r"(col_base + 32 * ci), "r"(y0)
-                : "memory");
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-          }
-        }
-        ostage += kBN / 32;
-      } else {
+      {
         // Each 128-byte-wide chunk of this warp's 32 rows is converted into
         // a swizzled staging buffer and written by one TMA tensor store
         // (rows past M are clipped by the tensor map), so global writes are
         // whole lines instead of one 16-byte piece per row per instruction.
-        constexpr int kCW = EPI == kEpiF32 ? 32 : 64;         // output columns per chunk
+        // kEpiResid (x += acc) stages the f32 accumulator the same way and
+        // issues a TMA reduce-add instead of the store: L2 adds it into x,
+        // one add per element, so nothing is loaded first.
+        constexpr bool kF32Out = EPI == kEpiF32 || EPI == kEpiResid;
+        constexpr int kCW = kF32Out ? 32 : 64;                // output columns per chunk
         constexpr int kOutCols = EPI == kEpiGeGLU ? kHalfN : kBN;
         const int col_base = nt * kOutCols;
         const int y0 = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + q * 32;
@@ -432,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           __syncwarp();
           uint8_t* srow = sbuf + lane * 128;
-          if (EPI == kEpiF32) {
+          if (kF32Out) {
             float v[32];
             tmem_ld_32x32b_x32(tb + c, v);
 #pragma unroll
@@ -464,11 +414,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            asm volatile(
-                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                    reinterpret_cast<uint64_t>(&tmOut)),
-                "r"(smem_u32(sbuf)), "r"(col_base + c), "r"(y0)
-                : "memory");
+            if (EPI == kEpiResid)
+              asm volatile(
+                  "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                      reinterpret_cast<uint64_t>(&tmOut)),
+                  "r"(smem_u32(sbuf)), "r"(col_base + c), "r"(y0)
+                  : "memory");
+            else
+              asm volatile(
+                  "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                      reinterpret_cast<uint64_t>(&tmOut)),
+                  "r"(smem_u32(sbuf)), "r"(col_base + c), "r"(y0)
+                  : "memory");
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
         }

@@ -15,7 +15,7 @@ bool gemm2_q4k_supports(int epi, int M, int N, int K);
 // Persistent launch over min(tiles, num_sms / 2) clusters of 2 CTAs.  `out`
 // is the TMA descriptor of the output matrix p.out ([M][ldo]; box 64 x 32
 // for f16 outputs, 32 x 32 for the f32 kEpiF32 / kEpiResid, 128-byte
-// swizzle); kEpiResid loads and stores the residual x through it.  w0 / w1
+// swizzle); kEpiResid adds into the residual x through it (TMA reduce-add).  w0 / w1
 // describe raw Q4_K rows (box kGemm2WBoxRows rows of super-blocks), or with
 // w_f16 the same weights dequantised to f16 [N][K] (box 64 x kGemm2WBoxRows,
 // 128-byte swizzle, like an activation map).
