@@ -87,6 +87,19 @@ int wc_t5_forward(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, 
 int wc_t5_forward_device(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengths, int B, int L, float* d_out,
                          float* d_norms, float* d_out_normalised, void* stream);
 
+/* n batches through the same forward as wc_t5_forward, pipelined: while
+ * batch i runs, batch i's predecessor's results are copied out and batch
+ * i + 2's inputs copied in (a second stream and two device I/O buffer sets),
+ * so with page-locked host buffers the copies hide behind the compute.
+ * ids[i] / lengths[i] (lengths may be NULL, or lengths[i] NULL for full
+ * rows) / B[i] / L[i] / out[i] / norms[i] (norms may be NULL) as in
+ * wc_t5_forward; every result is the same as that batch's wc_t5_forward.
+ * Returns when all results are in host memory.  No reference counterpart:
+ * the reference embeds one document per call (src/embedder.rs:22-102); this
+ * is the entry for a batched caller. */
+int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, const int32_t* const* lengths, const int* B,
+                       const int* L, float* const* out, float* const* norms);
+
 /* Same computation as wc_t5_forward_device, for callers that must not
  * allocate GPU memory during a call: a real-time query path that cannot
  * afford cudaMalloc's implicit device synchronisation, or a host that owns

@@ -159,3 +159,19 @@ def test_graph_replay_matches_eager(xtr_gpu, xtr_oracle):
         _check(out, xtr_oracle.encode(ids, lengths), lengths)
     again = xtr_gpu.forward(runs[0][0], lengths)
     np.testing.assert_array_equal(again, runs[0][1])
+
+
+def test_forward_many_equals_single_calls(tiny_gpu):
+    """The pipelined entry point gives each batch exactly its wc_t5_forward result."""
+    rng = np.random.default_rng(21)
+    batches = []
+    for B, L in [(3, 40), (1, 7), (64, 20), (2, 300), (5, 33), (40, 64), (1, 1)]:
+        ids = rng.integers(3, 512, (B, L)).astype(np.uint32)  # tiny model: vocab 512
+        lens = rng.integers(1, L + 1, B).astype(np.int32)
+        batches.append((ids, lens))
+    for n in (len(batches), 2, 1):  # odd, even and single batch counts
+        got, gn = tiny_gpu.forward_many(batches[:n], with_norms=True)
+        for (ids, lens), o, nr in zip(batches[:n], got, gn):
+            ref, rn, _ = tiny_gpu.forward_full(ids, lens)
+            np.testing.assert_array_equal(o, ref)
+            np.testing.assert_array_equal(nr, rn)

@@ -160,6 +160,16 @@ struct wc_t5 {
   int32_t* d_len = nullptr;
   float *d_out = nullptr, *d_norms = nullptr, *d_outn = nullptr;
   uint32_t* d_status = nullptr;
+  // wc_t5_forward_many: two I/O buffer sets (ids, lengths, out, norms), a copy
+  // stream and its events, created on first use
+  uint8_t* io = nullptr;
+  int64_t io_rows = 0;
+  int io_b = 0;
+  uint32_t* io_ids[2] = {};
+  int32_t* io_len[2] = {};
+  float *io_out[2] = {}, *io_norms[2] = {};
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t ev_in[2] = {}, ev_fwd[2] = {}, ev_out[2] = {};
   // CUDA graphs of the kernel sequence for small batches, keyed by shape,
   // buffers and stream; an entry first records that the key was seen and is
   // captured on its second use.
@@ -391,6 +401,14 @@ extern "C" int wc_t5_destroy(wc_t5* h) {
     free_workspace(h);
     if (h->arena) cudaFree(h->arena);
     if (h->arena_f16) cudaFree(h->arena_f16);
+    if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
+    if (h->io) cudaFree(h->io);
+    for (int i = 0; i < 2; ++i) {
+      if (h->ev_in[i]) cudaEventDestroy(h->ev_in[i]);
+      if (h->ev_fwd[i]) cudaEventDestroy(h->ev_fwd[i]);
+      if (h->ev_out[i]) cudaEventDestroy(h->ev_out[i]);
+    }
+    if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
     if (h->d_status) cudaFree(h->d_status);
     if (h->stream) cudaStreamDestroy(h->stream);
   }
@@ -718,6 +736,141 @@ uint32_t* kernel_status_word() {
   return words[dev];
 }
 }  // namespace
+
+namespace wc {
+namespace {
+
+// Validates one host batch like wc_t5_forward and fills its lengths.
+int check_batch(wc_t5* h, const uint32_t* ids, const int32_t* lengths, int B, int L, const float* out,
+                std::vector<int32_t>& len) {
+  if (!ids || !out || B < 1 || L < 1 || L > kMaxL || static_cast<int64_t>(B) * L > (1 << 26))
+    return fail(h, WC_E_INVALID_ARG, "invalid ids/out pointer or B, L out of range (1 <= L <= 2048)");
+  len.assign(B, L);
+  if (lengths) {
+    for (int b = 0; b < B; ++b) {
+      if (lengths[b] < 1 || lengths[b] > L)
+        return fail(h, WC_E_INVALID_ARG, "lengths[" + std::to_string(b) + "] is outside [1, L]");
+      len[b] = lengths[b];
+    }
+  }
+  for (int b = 0; b < B; ++b)
+    for (int i = 0; i < len[b]; ++i)
+      if (ids[static_cast<size_t>(b) * L + i] >= static_cast<uint32_t>(h->cfg.vocab_size))
+        return fail(h, WC_E_INVALID_ARG, "token id " + std::to_string(ids[static_cast<size_t>(b) * L + i]) +
+                                             " is not below vocab_size " + std::to_string(h->cfg.vocab_size));
+  return WC_OK;
+}
+
+int ensure_io(wc_t5* h, int64_t rows, int B) {
+  if (!h->copy_stream) {
+    cudaError_t e = cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking);
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+      if ((e = cudaEventCreateWithFlags(&h->ev_in[i], cudaEventDisableTiming)) == cudaSuccess &&
+          (e = cudaEventCreateWithFlags(&h->ev_fwd[i], cudaEventDisableTiming)) == cudaSuccess)
+        e = cudaEventCreateWithFlags(&h->ev_out[i], cudaEventDisableTiming);
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "copy stream / events");
+  }
+  if (rows <= h->io_rows && B <= h->io_b) return WC_OK;
+  clear_graphs(h);  // captured graphs may hold the old I/O pointers
+  if (h->io) {
+    cudaStreamSynchronize(h->stream);
+    cudaStreamSynchronize(h->copy_stream);
+    cudaFree(h->io);
+    h->io = nullptr;
+  }
+  const int64_t cap = std::max<int64_t>((rows + 127) / 128 * 128, h->io_rows);
+  const int capb = std::max(B, h->io_b);
+  const size_t P = h->d_proj;
+  size_t off = 0, o_ids[2], o_len[2], o_out[2], o_norms[2];
+  for (int i = 0; i < 2; ++i) {
+    o_ids[i] = off; off = align256(off + cap * 4);
+    o_len[i] = off; off = align256(off + capb * 4);
+    o_out[i] = off; off = align256(off + cap * P * 4);
+    o_norms[i] = off; off = align256(off + cap * 4);
+  }
+  cudaError_t e = cudaMalloc(&h->io, off);
+  if (e != cudaSuccess) {
+    h->io = nullptr;
+    h->io_rows = 0;
+    h->io_b = 0;
+    return cuda_fail(h, e, "I/O buffer allocation");
+  }
+  for (int i = 0; i < 2; ++i) {
+    h->io_ids[i] = reinterpret_cast<uint32_t*>(h->io + o_ids[i]);
+    h->io_len[i] = reinterpret_cast<int32_t*>(h->io + o_len[i]);
+    h->io_out[i] = reinterpret_cast<float*>(h->io + o_out[i]);
+    h->io_norms[i] = reinterpret_cast<float*>(h->io + o_norms[i]);
+  }
+  h->io_rows = cap;
+  h->io_b = capb;
+  return WC_OK;
+}
+
+}  // namespace
+}  // namespace wc
+
+extern "C" int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, const int32_t* const* lengths,
+                                  const int* B, const int* L, float* const* out, float* const* norms) {
+  if (!h) return WC_E_INVALID_ARG;
+  if (n < 0 || (n > 0 && (!ids || !B || !L || !out)))
+    return fail(h, WC_E_INVALID_ARG, "invalid batch arrays");
+  if (n == 0) return WC_OK;
+  std::vector<std::vector<int32_t>> lens(n);
+  int64_t max_rows = 0;
+  int max_b = 0;
+  for (int i = 0; i < n; ++i) {
+    const int rc = check_batch(h, ids[i], lengths ? lengths[i] : nullptr, B[i], L[i], out[i], lens[i]);
+    if (rc) return rc;
+    max_rows = std::max<int64_t>(max_rows, static_cast<int64_t>(B[i]) * L[i]);
+    max_b = std::max(max_b, B[i]);
+  }
+  DeviceGuard g(h->device);
+  int rc = ensure_workspace(h, max_rows, max_b);
+  if (!rc) rc = ensure_io(h, max_rows, max_b);
+  if (rc) return rc;
+  cudaStream_t cs = h->stream, ps = h->copy_stream;
+  cudaError_t e = cudaMemsetAsync(h->d_status, 0, 4, cs);
+  auto upload = [&](int i) -> cudaError_t {
+    const int s = i & 1;
+    const int64_t M = static_cast<int64_t>(B[i]) * L[i];
+    cudaError_t r = cudaMemcpyAsync(h->io_ids[s], ids[i], M * 4, cudaMemcpyHostToDevice, ps);
+    if (r == cudaSuccess) r = cudaMemcpyAsync(h->io_len[s], lens[i].data(), B[i] * 4, cudaMemcpyHostToDevice, ps);
+    if (r == cudaSuccess) r = cudaEventRecord(h->ev_in[s], ps);
+    return r;
+  };
+  for (int i = 0; i < 2 && i < n && e == cudaSuccess; ++i) e = upload(i);
+  for (int i = 0; i < n && e == cudaSuccess && rc == WC_OK; ++i) {
+    const int s = i & 1;
+    const int64_t M = static_cast<int64_t>(B[i]) * L[i];
+    float* nrm = norms ? norms[i] : nullptr;
+    // compute: inputs of batch i landed; d_out of set s read out (batch i - 2)
+    if ((e = cudaStreamWaitEvent(cs, h->ev_in[s], 0)) != cudaSuccess) break;
+    if (i >= 2 && (e = cudaStreamWaitEvent(cs, h->ev_out[s], 0)) != cudaSuccess) break;
+    rc = forward_cached(h, h->io_ids[s], h->io_len[s], B[i], L[i], h->io_out[s], nrm ? h->io_norms[s] : nullptr,
+                        nullptr, cs);
+    if (rc) break;
+    if ((e = cudaEventRecord(h->ev_fwd[s], cs)) != cudaSuccess) break;
+    // copy: results of batch i out, then inputs of batch i + 2 into set s
+    if ((e = cudaStreamWaitEvent(ps, h->ev_fwd[s], 0)) != cudaSuccess) break;
+    if ((e = cudaMemcpyAsync(out[i], h->io_out[s], M * h->d_proj * 4, cudaMemcpyDeviceToHost, ps)) != cudaSuccess)
+      break;
+    if (nrm && (e = cudaMemcpyAsync(nrm, h->io_norms[s], M * 4, cudaMemcpyDeviceToHost, ps)) != cudaSuccess) break;
+    if ((e = cudaEventRecord(h->ev_out[s], ps)) != cudaSuccess) break;
+    if (i + 2 < n && (e = upload(i + 2)) != cudaSuccess) break;
+  }
+  const cudaError_t es = cudaStreamSynchronize(ps);
+  if (rc) {
+    cudaStreamSynchronize(cs);
+    return rc;
+  }
+  if (e == cudaSuccess) e = es;
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(cs);
+    return cuda_fail(h, e, "pipelined forward");
+  }
+  return check_status(h, cs);
+}
 
 extern "C" int wc_q4k_dequant_f16(const void* d_blocks, int64_t nblocks, void* d_out_f16, void* stream) {
   if (nblocks < 0 || (nblocks > 0 && (!d_blocks || !d_out_f16))) return WC_E_INVALID_ARG;

@@ -85,6 +85,23 @@ class T5EncoderModel:
         check(lib().wc_t5_forward(self._h, _ptr(ids), _ptr(lens), B, L, _ptr(out), None, None), self._h)
         return out
 
+    def forward_many(self, batches, with_norms: bool = False):
+        """[(ids [B, L] u32, lengths [B] or None)] -> [raw [B, L, 128]] (and norms),
+        pipelined through wc_t5_forward_many (copies overlap the compute when
+        the arrays are page-locked)."""
+        n = len(batches)
+        ids = [np.ascontiguousarray(np.atleast_2d(b[0]), dtype=np.uint32) for b in batches]
+        lens = [None if b[1] is None else np.ascontiguousarray(b[1], dtype=np.int32) for b in batches]
+        outs = [np.empty((a.shape[0], a.shape[1], self.d_proj), np.float32) for a in ids]
+        norms = [np.empty(a.shape, np.float32) for a in ids] if with_norms else None
+        vp = ctypes.c_void_p
+        arr = lambda xs: (vp * n)(*[vp(x.ctypes.data) if x is not None else None for x in xs])  # noqa: E731
+        Bs = (ctypes.c_int * n)(*[a.shape[0] for a in ids])
+        Ls = (ctypes.c_int * n)(*[a.shape[1] for a in ids])
+        check(lib().wc_t5_forward_many(self._h, n, arr(ids), arr(lens), Bs, Ls, arr(outs),
+                                       arr(norms) if norms is not None else None), self._h)
+        return (outs, norms) if with_norms else outs
+
     def forward_device(self, d_ids: int, d_lengths: int, B: int, L: int, d_out: int, d_norms: int | None = None,
                        d_outn: int | None = None, stream: int | None = None) -> None:
         """Enqueue a forward on device buffers (raw pointers) on `stream`."""
