@@ -94,6 +94,14 @@ def test_xtr_query_shapes(xtr_gpu, xtr_oracle):
     _check(xtr_gpu.forward(ids, lengths), xtr_oracle.encode(ids, lengths), lengths)
 
 
+@pytest.mark.parametrize("B,L,lengths", [(1, 32, [32]), (1, 20, [13]), (2, 16, [16, 5])])
+def test_xtr_small_batch_path(xtr_gpu, xtr_oracle, B, L, lengths):
+    """B * L <= 32 tokens: the small-M layer path (input RMSNorm inside the
+    QKV / gated-FF GEMMs, residual adds inside the O / wo GEMMs)."""
+    ids = np.random.default_rng(B * 100 + L).integers(3, 32128, (B, L)).astype(np.uint32)
+    _check(xtr_gpu.forward(ids, lengths), xtr_oracle.encode(ids, lengths), lengths)
+
+
 def test_long_window_tiny(tiny_gpu, tiny_model):
     ids = np.random.default_rng(8).integers(3, 512, (1, 2048)).astype(np.uint32)
     _check(tiny_gpu.forward(ids), O.OracleEncoder(tiny_model).encode(ids), [2048])

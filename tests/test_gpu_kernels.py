@@ -100,7 +100,7 @@ def test_gemm_geglu(M, K, F):
     assert err < 5e-3, err
 
 
-@pytest.mark.parametrize("M", [333, 4000])
+@pytest.mark.parametrize("M", [1, 7, 32, 333, 4000])
 def test_gemm_residual_accumulates(M):
     K, N = 2048, 768
     blocks, wd = _weights(N, K, 12)
