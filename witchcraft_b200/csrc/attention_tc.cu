@@ -39,6 +39,24 @@ namespace wc {
 
 namespace {
 
+// Optional event trace for pipeline analysis (off in the library build):
+// single threads of the first kTraceCtas CTAs log (event code, SM clock).
+#ifdef WC_ATTN_TRACE
+constexpr int kTraceCtas = 16, kTraceLen = 8192, kTraceRole = kTraceLen / 8;
+__device__ unsigned long long g_attn_trace[kTraceCtas][kTraceLen];
+#define ATRACE(code)                                                                                    \
+  do {                                                                                                  \
+    if (blockIdx.x < kTraceCtas && tr_n < kTraceRole)                                                   \
+      g_attn_trace[blockIdx.x][(threadIdx.x >> 5) * kTraceRole + tr_n++] =   \
+          (static_cast<unsigned long long>(code) << 56) |                                               \
+          (static_cast<unsigned long long>(clock64()) & ((1ull << 56) - 1));                            \
+  } while (0)
+#else
+#define ATRACE(code) \
+  do {               \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -133,10 +151,15 @@ static_assert(kBiasPad >= kMaxL + kWin + 1 && kBiasPad % 32 == 16, "bias row cop
 constexpr int kOffBias = kOffV + kKVStages * kKVBytes;  // f32 [2 copies][kBiasPad]
 constexpr int kOffTab = kOffBias + 2 * kBiasPad * 4;   // f32 [kMaxHeads][64]
 constexpr int kOffThr = kOffTab + kMaxHeads * 64 * 4;  // int [32]
-constexpr int kMaxSortSeqs = 4096;  // larger batches keep their own sequence order
-constexpr int kOffOrder = kOffThr + 32 * 4;            // u16 [kMaxSortSeqs]
-constexpr int kOffHist = kOffOrder + kMaxSortSeqs * 2;                   // int [64]
-constexpr int kOffBar = kOffHist + 64 * 4;
+constexpr int kMaxSortSeqs = 2048;  // larger batches keep their own sequence order
+constexpr int kOffOrder = kOffThr + 32 * 4;            // u32 [kMaxSortSeqs]: b | length << 16
+constexpr int kOffHist = kOffOrder + kMaxSortSeqs * 4;                   // int [64]
+// bucket of every key - query offset an item's bias row can need: index
+// delta + kBktHalf, |delta| <= kMaxL + kWin
+constexpr int kBktHalf = kMaxL + kWin;
+constexpr int kOffBkt = kOffHist + 64 * 4;                               // u8 [2 kBktHalf + 1]
+constexpr int kOffStage = kOffBkt + ((2 * kBktHalf + 1 + 127) & ~127);   // [4 warps][32 rows][64 B]
+constexpr int kOffBar = kOffStage + 4 * 32 * 64;
 constexpr int kSmem = 1024 + kOffBar + 256;
 constexpr int kThreads = 192;
 constexpr int kCtasPerSm = 2;
@@ -156,7 +179,7 @@ struct Item {
 
 struct ItemList {
   const int32_t* lengths;
-  const uint16_t* order;  // sorted sequence index, or null: identity
+  const uint32_t* order;  // sorted (sequence | length << 16), or null: identity
   int n_items, q_tiles, H, L;
 
   __device__ __forceinline__ int seq_len(int b) const { return max(0, min(lengths[b], L)); }
@@ -169,8 +192,14 @@ struct ItemList {
     const int rest = id / H;
     it.q0 = (rest % q_tiles) * kQ;
     const int pos = rest / q_tiles;
-    it.b = order ? order[pos] : pos;
-    it.len = seq_len(it.b);
+    if (order) {
+      const uint32_t e = order[pos];
+      it.b = static_cast<int>(e & 0xFFFFu);
+      it.len = static_cast<int>(e >> 16);
+    } else {
+      it.b = pos;
+      it.len = seq_len(pos);
+    }
     it.n_kt = (it.len + kKeys - 1) / kKeys;
     return it;
   }
@@ -198,8 +227,9 @@ struct Cursor {
 };
 
 // One warp: order[pos] = the sequences by descending key-tile count, ties in
-// index order (a stable counting sort, so every CTA gets the same order).
-__device__ void sort_sequences(const ItemList& il, int B, uint16_t* order, int* hist, int lane) {
+// index order (a stable counting sort, so every CTA gets the same order),
+// each with its clamped length, so no later step reads the lengths again.
+__device__ void sort_sequences(const ItemList& il, int B, uint32_t* order, int* hist, int lane) {
   constexpr int kBins = kMaxL / kKeys + 1;
   for (int i = lane; i < 64; i += 32) hist[i] = 0;
   __syncwarp();
@@ -221,9 +251,12 @@ __device__ void sort_sequences(const ItemList& il, int B, uint16_t* order, int* 
   __syncwarp();
   for (int b0 = 0; b0 < B; b0 += 32) {
     const int b = b0 + lane;
-    const int key = b < B ? (il.seq_len(b) + kKeys - 1) / kKeys : -1;
+    const int len = b < B ? il.seq_len(b) : 0;
+    const int key = b < B ? (len + kKeys - 1) / kKeys : -1;
     const unsigned same = __match_any_sync(0xFFFFFFFFu, key);
-    if (key >= 0) order[hist[key] + __popc(same & ((1u << lane) - 1u))] = static_cast<uint16_t>(b);
+    if (key >= 0)
+      order[hist[key] + __popc(same & ((1u << lane) - 1u))] =
+          static_cast<uint32_t>(b) | (static_cast<uint32_t>(len) << 16);
     __syncwarp();
     if (key >= 0 && lane == __ffs(same) - 1) hist[key] += __popc(same);
     __syncwarp();
@@ -264,9 +297,13 @@ __global__ void __launch_bounds__(kThreads)
 
   pdl_wait();  // before lengths and any activation (see pdl_wait)
   pdl_launch_next();  // after the wait: at most one grid waits ahead
+#ifdef WC_ATTN_TRACE
+  int tr_n = 0;
+#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_tiles = (L + kQ - 1) / kQ;
-  uint16_t* sOrder = reinterpret_cast<uint16_t*>(smem + kOffOrder);
+  uint32_t* sOrder = reinterpret_cast<uint32_t*>(smem + kOffOrder);
+  uint8_t* sBkt = smem + kOffBkt;
   const ItemList il{lengths, B <= kMaxSortSeqs ? sOrder : nullptr, B * q_tiles * H, q_tiles, H, L};
   const int inner = H * kDh;
 
@@ -310,6 +347,7 @@ __global__ void __launch_bounds__(kThreads)
       // Q of the g-th active item (single buffer, free once the previous Q is in TMEM)
       auto load_q = [&](const Item& it, int g) -> bool {
         if (!mbar_wait(q_empty, (g & 1) ^ 1, status)) return false;
+        ATRACE(22);
         mbar_arrive_expect_tx(q_full, kQBytes);
         const int row = it.b * L + it.q0;
         tma_load_2d(sQ, &tmQKV, q_full, it.h * kDh, row);  // box: 64 rows
@@ -328,9 +366,11 @@ __global__ void __launch_bounds__(kThreads)
         const uint32_t par = ((t / kKVStages) & 1) ^ 1;
         const int krow = c.it.b * L + c.j * kKeys;
         if (!(ok = mbar_wait(&k_empty[s], par, status))) break;
+        ATRACE(20);
         mbar_arrive_expect_tx(&k_full[s], kKVBytes);
         tma_load_2d(sK + s * kKVBytes, &tmQKV, &k_full[s], inner + c.it.h * kDh, krow);
         if (!(ok = mbar_wait(&v_empty[s], par, status))) break;
+        ATRACE(21);
         mbar_arrive_expect_tx(&v_full[s], kKVBytes);
         tma_load_2d(sV + s * kKVBytes, &tmQKV, &v_full[s], 2 * inner + c.it.h * kDh, krow);
         c.advance(il);
@@ -356,6 +396,7 @@ __global__ void __launch_bounds__(kThreads)
         for (int k = 0; k < kDh / 16; ++k)
           tc_mma_f16_ts(tmem + kColS + 64 * (ts & 1), qa + 8 * k, bk + 2 * k, idesc_qk, k > 0);
         tc_commit(&s_full[ts & 1]);
+        ATRACE(12);
         tc_commit(&k_empty[s]);
         cs.advance(il);
         ++ts;
@@ -367,6 +408,7 @@ __global__ void __launch_bounds__(kThreads)
         const int s = t % kKVStages;
         // P(t) also means the epilogue of the previous item has read O
         if (!(ok = mbar_wait(&p_full[t & 1], (t >> 1) & 1, status))) break;
+        ATRACE(10);
         if (!(ok = mbar_wait(&v_full[s], (t / kKVStages) & 1, status))) break;
         tc_fence_after();
         const uint64_t v = sw128_mnmajor_desc(smem_u32(sV + s * kKVBytes));
@@ -375,6 +417,7 @@ __global__ void __launch_bounds__(kThreads)
         for (int k = 0; k < kKeys / 16; ++k)
           tc_mma_f16_ts(tmem + kColO, pa + 8 * k, v + 128 * k, idesc_pv, (cp.j > 0 || k > 0) ? 1u : 0u);
         tc_commit(&o_done[t & 1]);
+        ATRACE(11);
         tc_commit(&v_empty[s]);
         cp.advance(il);
         if (cs.valid(il)) ok = issue_s();  // S buffer t % 2 is free again
@@ -384,6 +427,12 @@ __global__ void __launch_bounds__(kThreads)
     // ------------------------------------------------------------ softmax + epilogue
     const int st = threadIdx.x - 64;  // 0..127
     const int qd = warp & 3;          // TMEM lane quarter
+    // buckets of the offsets this launch can meet (|delta| < L + kWin); the
+    // first item's barrier below orders these writes before their use
+    for (int i = st; i < 2 * (L + kWin) - 1; i += 128) {
+      const int delta = i - (L + kWin - 1);
+      sBkt[delta + kBktHalf] = static_cast<uint8_t>(rel_bucket_tc(sThr, bt.half, delta));
+    }
     const int r = qd * 32 + lane;     // query row within the tile
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     // Q of the g-th active item: shared memory (TMA, 128-B swizzle) -> this
@@ -426,28 +475,33 @@ __global__ void __launch_bounds__(kThreads)
         }
         continue;
       }
+      if (lane == 0) ATRACE(1);
       if (g == 0 && ok) ok = stage_q(0);
       // one item ahead: Q buffer (g + 1) % 2 last served item g - 1, whose
       // S tiles this thread has all consumed
       if (ok && il.next_active(round + 1).id < il.n_items) ok = stage_q(g + 1);
       // bias row of this item (after every softmax thread has finished the
       // previous one's steps)
+      if (lane == 0) ATRACE(2);
       asm volatile("bar.sync 1, 128;" ::: "memory");
       {
         const float* tab = sTab + it.h * 64;
+        const uint8_t* bk = sBkt + kBktHalf - it.q0 - (kQ - 1);
         for (int x = st; x < it.n_kt * kKeys + kWin; x += 128) {
-          const float w = tab[rel_bucket_tc(sThr, bt.half, x - it.q0 - (kQ - 1))];
+          const float w = tab[bk[x]];
           sBias[x] = w;
           if (x > 0) sBias[kBiasPad + x - 1] = w;
         }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (lane == 0) ATRACE(3);
       // bias of key c at brow[c], brow 8-byte aligned
       const float* brow = ((kQ - 1 - r) & 1) ? sBias + kBiasPad + (kQ - 2 - r) : sBias + (kQ - 1 - r);
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < it.n_kt; ++j, ++t) {
         const int k0 = j * kKeys;
         if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[t & 1], (t >> 1) & 1, status));
+        if (lane == 0) ATRACE(4);
         if (ok) {
           tc_fence_after();
           float v[kKeys];
@@ -515,32 +569,46 @@ __global__ void __launch_bounds__(kThreads)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t & 1]);
+        if (lane == 0) ATRACE(5);
       }
       // epilogue of the item: O / l -> f16 (the next P V overwrites O only
       // after this thread's next arrival on p_full)
       if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, status));
+      if (lane == 0) ATRACE(6);
       if (ok) {
         tc_fence_after();
         const float inv = 1.0f / l_run;
         const uint32_t ocol = trow + kColO;
+        // each 32-column half of the warp's 32 rows goes through a 2 KB
+        // staging tile (16-byte chunks XOR-swizzled by row, conflict-free both
+        // ways), so every store instruction writes 8 rows x 64 contiguous bytes
+        uint8_t* stage = smem + kOffStage + qd * 2048;
+        const int rq0 = it.q0 + qd * 32;  // first query row of this warp
 #pragma unroll 1
         for (int c = 0; c < kDh; c += 32) {
           float o[32];
           tmem_ld_32x32b_x32(ocol + c, o);
-          if (qi < L) {
-            __half* dst = out + (row0 + qi) * inner + it.h * kDh + c;
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 w;
-              w.x = pack_f16x2_sat(o[i] * inv, o[i + 1] * inv);
-              w.y = pack_f16x2_sat(o[i + 2] * inv, o[i + 3] * inv);
-              w.z = pack_f16x2_sat(o[i + 4] * inv, o[i + 5] * inv);
-              w.w = pack_f16x2_sat(o[i + 6] * inv, o[i + 7] * inv);
-              *reinterpret_cast<uint4*>(dst + i) = w;
-            }
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack_f16x2_sat(o[i] * inv, o[i + 1] * inv);
+            w.y = pack_f16x2_sat(o[i + 2] * inv, o[i + 3] * inv);
+            w.z = pack_f16x2_sat(o[i + 4] * inv, o[i + 5] * inv);
+            w.w = pack_f16x2_sat(o[i + 6] * inv, o[i + 7] * inv);
+            *reinterpret_cast<uint4*>(stage + lane * 64 + 16 * ((i >> 3) ^ ((lane >> 1) & 3))) = w;
           }
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int rr = k * 8 + (lane >> 2), ch = lane & 3;
+            const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * 64 + 16 * (ch ^ ((rr >> 1) & 3)));
+            if (rq0 + rr < L)
+              *reinterpret_cast<uint4*>(out + (row0 + rq0 + rr) * inner + it.h * kDh + c + ch * 8) = w;
+          }
+          __syncwarp();
         }
       }
+      if (lane == 0) ATRACE(7);
       ++g;
     }
   }
@@ -555,6 +623,20 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 }  // namespace
+
+#ifdef WC_ATTN_TRACE
+extern "C" int wc_attn_trace_reset() {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_attn_trace);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(unsigned long long) * kTraceCtas * kTraceLen);
+  return static_cast<int>(e);
+}
+extern "C" int wc_attn_trace_read(unsigned long long* events, unsigned* counts) {
+  (void)counts;
+  return static_cast<int>(
+      cudaMemcpyFromSymbol(events, g_attn_trace, sizeof(unsigned long long) * kTraceCtas * kTraceLen));
+}
+#endif
 
 cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const int32_t* lengths, int B, int L, int H,
                                 const float* bias_tab, const BucketThresholds& bt, uint32_t* status,
