@@ -337,11 +337,15 @@ def _time_launches(fn, stream, reps: int, warm: int = 3) -> float:
             fn()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
     with torch.cuda.stream(stream):
+        # a device-side delay ahead of the timed launches lets the host queue
+        # all of them first, so host launch overhead cannot open gaps between
+        # short kernels inside the timed region
+        torch.cuda._sleep(20_000_000)
+        a.record(stream)
         for _ in range(reps):
             fn()
-    b.record(stream)
+        b.record(stream)
     torch.cuda.synchronize()
     return a.elapsed_time(b) / reps / 1e3  # seconds per launch
 

@@ -10,23 +10,22 @@
 // MMAs of the next step -- also across an item boundary -- overlap the
 // softmax of the current one, and the set-up (barriers, TMEM, the bias
 // tables of all heads) is paid once per CTA:
-//   warp 0      TMA: the Q tile of each head (one shared-memory buffer),
-//               its K and V tiles (two 3-stage rings; a K stage is freed as
-//               soon as its S is done)
+//   warp 0      TMA: the Q tile of each item (two shared-memory buffers,
+//               one item ahead), its K and V tiles (two 2-stage rings; a K
+//               stage is freed as soon as its S is done)
 //   warp 1      TMEM allocation and the single MMA-issuing thread
-//   warps 2-5   Q staging, softmax and epilogue (thread = query row = TMEM lane)
-// Shared-memory bandwidth bounds this kernel at d = 64, so both A operands
-// live in tensor memory: the softmax warps copy each head's Q tile into one
-// of two TMEM Q buffers (one head ahead), and write P as f16 over the S
-// buffer it came from.  Step t (head h, key tile j): S(t) = Q_h K_j^T (M=128,
-// N=64, K=64, A from TMEM, f32 in TMEM buffer t % 2, computed ahead); the
-// softmax warps add the relative-position bias (a per-tile window of 191
-// biases they build), mask keys past the sequence, update the running max /
-// sum, rescale the O row in TMEM when the max moved and store P = 2^(S - max)
-// into the first 32 columns of S buffer t % 2; then O += P V_j (M=128, N=64,
-// K=64, A = P from TMEM, V read MN-major from its TMA tile).  S(t + 2) reuses
-// that buffer only after P(t) V(t), in MMA issue order.  One O buffer
-// suffices: the same warps read it out before they release the next P.
+//   warps 2-5   softmax and epilogue (thread = query row = TMEM lane)
+// Step t (item g, key tile j): S(t) = Q K_j^T (M=128, N=64, K=64, Q and K
+// K-major from their TMA tiles, f32 in TMEM buffer t % 2, computed two steps
+// ahead); the softmax warps add the relative-position bias (a per-item bias
+// row they build), mask keys past the sequence, update the running max / sum,
+// rescale the O row in TMEM when the max moved and store P = 2^(S - max) as
+// f16 into the first 32 columns of S buffer t % 2; then O_g += P V_j (M=128,
+// N=64, K=64, A = P from TMEM, V read MN-major from its TMA tile).  S(t + 2)
+// reuses that buffer only after P(t) V(t), in MMA issue order.  O has two
+// TMEM buffers (item g in buffer g % 2), so the epilogue of item g (O / sum
+// -> f16 -> global) runs after the first step of item g + 1, when its last
+// P V has long finished, instead of waiting for it.
 // Input: the token-major QKV projection [B*L][3*H*64] f16 through one TMA
 // descriptor (box 64 x 64); output [B*L][H*64] f16.  Query rows of an
 // all-padding tile are written as zeros.
@@ -51,7 +50,16 @@ __device__ unsigned long long g_attn_trace[kTraceCtas][kTraceLen];
           (static_cast<unsigned long long>(code) << 56) |                                               \
           (static_cast<unsigned long long>(clock64()) & ((1ull << 56) - 1));                            \
   } while (0)
+#define ATRACE_NS(code)                                                                              \
+  do {                                                                                               \
+    if (blockIdx.x < kTraceCtas && threadIdx.x == 0)                                                 \
+      g_attn_trace[blockIdx.x][7 * kTraceRole + (code & 1)] =                                        \
+          (static_cast<unsigned long long>(code) << 56) | (global_timer_ns() & ((1ull << 56) - 1));   \
+  } while (0)
 #else
+#define ATRACE_NS(code) \
+  do {                  \
+  } while (0)
 #define ATRACE(code) \
   do {               \
   } while (0)
@@ -136,9 +144,9 @@ constexpr int kQBytes = kQ * 128;      // 128 x 64 f16
 constexpr int kKVBytes = kKeys * 128;  // 64 x 64 f16
 constexpr int kWin = kQ + kKeys - 1;   // distinct key - query offsets of one tile pair
 constexpr int kMaxHeads = 32;          // bias tables of all heads stay in shared memory
-constexpr int kKVStages = 3;
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;                // kKVStages stages
+constexpr int kKVStages = 2;
+constexpr int kOffQ = 0;                              // 2 buffers
+constexpr int kOffK = kOffQ + 2 * kQBytes;            // kKVStages stages
 constexpr int kOffV = kOffK + kKVStages * kKVBytes;   // kKVStages stages
 constexpr int kMaxL = 2048;
 // Bias row of one item: bias[x] for key - query = x - q0 - (kQ - 1), built
@@ -164,8 +172,8 @@ constexpr int kSmem = 1024 + kOffBar + 256;
 constexpr int kThreads = 192;
 constexpr int kCtasPerSm = 2;
 constexpr uint32_t kTmemCols = 256;
-// S (and P) buffers at 0 / 64, O at 128, Q buffers at 192 / 224
-constexpr uint32_t kColS = 0, kColO = 128, kColQ = 192;
+// S (and P) buffers at 0 / 64, O buffers at 128 / 192
+constexpr uint32_t kColS = 0, kColO = 128;
 
 // One unit of work: the kQ queries from q0 of sequence b, head h.  Items
 // are numbered with the sequences in descending order of key tiles (the
@@ -268,6 +276,7 @@ __global__ void __launch_bounds__(kThreads)
                         const int32_t* __restrict__ lengths, int B, int L, int H,
                         const float* __restrict__ bias_tab, BucketThresholds bt, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
+  ATRACE_NS(30);
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + kOffQ;
   uint8_t* sK = smem + kOffK;
@@ -276,24 +285,23 @@ __global__ void __launch_bounds__(kThreads)
   float* sTab = reinterpret_cast<float*>(smem + kOffTab);  // [head][bucket] * log2(e)
   int* sThr = reinterpret_cast<int*>(smem + kOffThr);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars;          // [1]
-  uint64_t* q_empty = bars + 1;     // [1] (4 softmax warps arrive once Q is in TMEM)
-  uint64_t* k_full = bars + 2;      // [kKVStages]
-  uint64_t* k_empty = bars + 5;     // [kKVStages]  freed when S(t) is done
-  uint64_t* v_full = bars + 8;      // [kKVStages]
-  uint64_t* v_empty = bars + 11;    // [kKVStages]  freed when P(t) V(t) is done
-  uint64_t* s_full = bars + 14;     // [2] per S buffer
+  uint64_t* q_full = bars;                        // [2] per Q buffer
+  uint64_t* q_empty = bars + 2;                   // [2] the item's last S is done
+  uint64_t* k_full = bars + 4;                    // [kKVStages]
+  uint64_t* k_empty = k_full + kKVStages;         // [kKVStages]  freed when S(t) is done
+  uint64_t* v_full = k_empty + kKVStages;         // [kKVStages]
+  uint64_t* v_empty = v_full + kKVStages;         // [kKVStages]  freed when P(t) V(t) is done
+  uint64_t* s_full = v_empty + kKVStages;         // [2] per S buffer
   // [2] by step parity (4 softmax warps arrive): the warps do not step in
   // lockstep, one may arrive for step t + 1 before another for step t, but
   // never for t + 2 (S(t + 2) is issued only after P(t))
-  uint64_t* p_full = bars + 16;
+  uint64_t* p_full = s_full + 2;
   // [2] by step parity: P(t) V(t) done.  A softmax warp waits for P V of step
-  // t or t - 1 while only P V(t - 2) is known complete (its S(t) came after
-  // it); one barrier per step parity keeps that wait one phase deep, which a
-  // parity wait tells apart.
-  uint64_t* o_done = bars + 18;
-  uint64_t* q_tm = bars + 20;       // [2] per TMEM Q buffer (4 softmax warps arrive)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  // t - 1 (rescale, epilogue) while P V(t + 1) cannot have been issued (it
+  // needs this warp's P(t + 1)); one barrier per step parity keeps that wait
+  // one phase deep, which a parity wait tells apart.
+  uint64_t* o_done = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   pdl_wait();  // before lengths and any activation (see pdl_wait)
   pdl_launch_next();  // after the wait: at most one grid waits ahead
@@ -308,8 +316,6 @@ __global__ void __launch_bounds__(kThreads)
   const int inner = H * kDh;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 4);
     for (int i = 0; i < kKVStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -317,8 +323,9 @@ __global__ void __launch_bounds__(kThreads)
       mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&q_tm[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
     }
@@ -344,14 +351,16 @@ __global__ void __launch_bounds__(kThreads)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      // Q of the g-th active item (single buffer, free once the previous Q is in TMEM)
+      // Q of the g-th active item into buffer g % 2 (free once the last S
+      // of item g - 2 is done)
       auto load_q = [&](const Item& it, int g) -> bool {
-        if (!mbar_wait(q_empty, (g & 1) ^ 1, status)) return false;
+        if (!mbar_wait(&q_empty[g & 1], ((g >> 1) & 1) ^ 1, status)) return false;
         ATRACE(22);
-        mbar_arrive_expect_tx(q_full, kQBytes);
+        uint8_t* dst = sQ + (g & 1) * kQBytes;
+        mbar_arrive_expect_tx(&q_full[g & 1], kQBytes);
         const int row = it.b * L + it.q0;
-        tma_load_2d(sQ, &tmQKV, q_full, it.h * kDh, row);  // box: 64 rows
-        tma_load_2d(sQ + kQBytes / 2, &tmQKV, q_full, it.h * kDh, row + 64);
+        tma_load_2d(dst, &tmQKV, &q_full[g & 1], it.h * kDh, row);  // box: 64 rows
+        tma_load_2d(dst + kQBytes / 2, &tmQKV, &q_full[g & 1], it.h * kDh, row + 64);
         return true;
       };
       Cursor c = start;
@@ -387,17 +396,20 @@ __global__ void __launch_bounds__(kThreads)
       // S(ts) = Q K_j^T into S buffer ts % 2 (needs its Q and K stage)
       auto issue_s = [&]() -> bool {
         const int s = ts % kKVStages;
-        if (cs.j == 0 && !mbar_wait(&q_tm[cs.g & 1], (cs.g >> 1) & 1, status)) return false;
+        if (cs.j == 0 && !mbar_wait(&q_full[cs.g & 1], (cs.g >> 1) & 1, status)) return false;
         if (!mbar_wait(&k_full[s], (ts / kKVStages) & 1, status)) return false;
+        ATRACE(15);
         tc_fence_after();
-        const uint32_t qa = tmem + kColQ + 32 * (cs.g & 1);
+        const uint64_t qa = sw128_kmajor_desc(smem_u32(sQ + (cs.g & 1) * kQBytes));
         const uint64_t bk = sw128_kmajor_desc(smem_u32(sK + s * kKVBytes));
 #pragma unroll
         for (int k = 0; k < kDh / 16; ++k)
-          tc_mma_f16_ts(tmem + kColS + 64 * (ts & 1), qa + 8 * k, bk + 2 * k, idesc_qk, k > 0);
+          tc_mma_f16(tmem + kColS + 64 * (ts & 1), qa + 2 * k, bk + 2 * k, idesc_qk, k > 0);
+        ATRACE(16);
         tc_commit(&s_full[ts & 1]);
         ATRACE(12);
         tc_commit(&k_empty[s]);
+        if (cs.j == cs.it.n_kt - 1) tc_commit(&q_empty[cs.g & 1]);
         cs.advance(il);
         ++ts;
         return true;
@@ -406,16 +418,19 @@ __global__ void __launch_bounds__(kThreads)
       Cursor cp = start;
       for (int t = 0; cp.valid(il) && ok; ++t) {
         const int s = t % kKVStages;
-        // P(t) also means the epilogue of the previous item has read O
+        // P(t) of item g also means the epilogue of item g - 2 has read O buffer g % 2
         if (!(ok = mbar_wait(&p_full[t & 1], (t >> 1) & 1, status))) break;
         ATRACE(10);
         if (!(ok = mbar_wait(&v_full[s], (t / kKVStages) & 1, status))) break;
+        ATRACE(13);
         tc_fence_after();
         const uint64_t v = sw128_mnmajor_desc(smem_u32(sV + s * kKVBytes));
         const uint32_t pa = tmem + kColS + 64 * (t & 1);
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k)
-          tc_mma_f16_ts(tmem + kColO, pa + 8 * k, v + 128 * k, idesc_pv, (cp.j > 0 || k > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem + kColO + 64 * (cp.g & 1), pa + 8 * k, v + 128 * k, idesc_pv,
+                        (cp.j > 0 || k > 0) ? 1u : 0u);
+        ATRACE(14);
         tc_commit(&o_done[t & 1]);
         ATRACE(11);
         tc_commit(&v_empty[s]);
@@ -435,28 +450,51 @@ __global__ void __launch_bounds__(kThreads)
     }
     const int r = qd * 32 + lane;     // query row within the tile
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-    // Q of the g-th active item: shared memory (TMA, 128-B swizzle) -> this
-    // thread's row of TMEM Q buffer g % 2, then release the shared buffer.
-    auto stage_q = [&](int g) -> bool {
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(q_full, g & 1, status))) return false;
-      uint32_t qr[32];
+    // Epilogue of an item whose O is final once P V of its last step t_last
+    // is done: O / sum -> f16 -> global.  Each 32-column half of the warp's 32
+    // rows goes through a 2 KB staging tile (16-byte chunks XOR-swizzled by
+    // row, conflict-free both ways), so every store instruction writes 8 rows
+    // x 64 contiguous bytes.
+    struct Pending {
+      size_t row0;
+      int q0, h, t_last, g;
+      float inv;
+    };
+    auto epilogue = [&](const Pending& e) -> bool {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&o_done[e.t_last & 1], (e.t_last >> 1) & 1, status))) return false;
+      tc_fence_after();
+      const uint32_t ocol = trow + kColO + 64 * (e.g & 1);
+      uint8_t* stage = smem + kOffStage + qd * 2048;
+      const int rq0 = e.q0 + qd * 32;  // first query row of this warp
+#pragma unroll 1
+      for (int c = 0; c < kDh; c += 32) {
+        float o[32];
+        tmem_ld_32x32b_x32(ocol + c, o);
+        if (lane == 0) ATRACE(8);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 w = *reinterpret_cast<const uint4*>(sQ + sw128_offset(r, c));
-        qr[4 * c] = w.x;
-        qr[4 * c + 1] = w.y;
-        qr[4 * c + 2] = w.z;
-        qr[4 * c + 3] = w.w;
-      }
-      tmem_st_u32_x32(trow + kColQ + 32 * (g & 1), qr);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(q_empty);
-        mbar_arrive(&q_tm[g & 1]);
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_f16x2_sat(o[i] * e.inv, o[i + 1] * e.inv);
+          w.y = pack_f16x2_sat(o[i + 2] * e.inv, o[i + 3] * e.inv);
+          w.z = pack_f16x2_sat(o[i + 4] * e.inv, o[i + 5] * e.inv);
+          w.w = pack_f16x2_sat(o[i + 6] * e.inv, o[i + 7] * e.inv);
+          *reinterpret_cast<uint4*>(stage + lane * 64 + 16 * ((i >> 3) ^ ((lane >> 1) & 3))) = w;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int rr = k * 8 + (lane >> 2), ch = lane & 3;
+          const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * 64 + 16 * (ch ^ ((rr >> 1) & 3)));
+          if (rq0 + rr < L)
+            *reinterpret_cast<uint4*>(out + (e.row0 + rq0 + rr) * inner + e.h * kDh + c + ch * 8) = w;
+        }
+        __syncwarp();
+        if (lane == 0) ATRACE(9);
       }
       return true;
     };
+    Pending pend{0, 0, 0, 0, 0, 0.f};
+    bool has_pend = false;
     bool ok = true;
     int t = 0, g = 0;
     for (int round = 0;; ++round) {
@@ -476,10 +514,6 @@ __global__ void __launch_bounds__(kThreads)
         continue;
       }
       if (lane == 0) ATRACE(1);
-      if (g == 0 && ok) ok = stage_q(0);
-      // one item ahead: Q buffer (g + 1) % 2 last served item g - 1, whose
-      // S tiles this thread has all consumed
-      if (ok && il.next_active(round + 1).id < il.n_items) ok = stage_q(g + 1);
       // bias row of this item (after every softmax thread has finished the
       // previous one's steps)
       if (lane == 0) ATRACE(2);
@@ -508,6 +542,7 @@ __global__ void __launch_bounds__(kThreads)
           tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1), &v[0]);
           tmem_ld_32x32b_x32_nowait(trow + kColS + 64 * (t & 1) + 32, &v[32]);
           tmem_wait_ld();
+          if (lane == 0) ATRACE(17);
           // v = S log2(e) + bias, two lanes per instruction; 4 max chains
           const uint64_t kLog2e2 = f2(1.4426950408889634f, 1.4426950408889634f);
           float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -527,9 +562,11 @@ __global__ void __launch_bounds__(kThreads)
           for (int i = 0; i < kKeys; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], v[i], v[i + 1]);
           const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
           // Lazy rescale: keep the running max unless this tile raises it by
-          // more than 8 (log2 units), so P stays <= 2^8 and O is rescaled
-          // rarely; the final division by the matching sum makes it exact.
-          const float m_new = (tmax > m_run + 8.0f) ? tmax : m_run;
+          // more than 15 (log2 units), so P stays <= 2^15 (f16 holds up to
+          // 65504 at the same relative precision) and O, whose rescale waits
+          // for the previous P V, is rescaled rarely; the final division by
+          // the matching sum makes it exact.
+          const float m_new = (tmax > m_run + 15.0f) ? tmax : m_run;
           const float corr = ex2(m_run - m_new);  // 1 when kept, 0 on the item's first tile
           // p = 2^(v - max) -> f16 P row over the first 32 columns of S buffer
           // t % 2 (S(t) is in registers), row sum in f32
@@ -543,7 +580,9 @@ __global__ void __launch_bounds__(kThreads)
             ps[(i >> 1) & 3] = f2_add(ps[(i >> 1) & 3], p);
             pk[i >> 1] = f2_to_h2(p);
           }
+          if (lane == 0) ATRACE(19);
           tmem_st_u32_x32(trow + kColS + 64 * (t & 1), pk);
+          if (lane == 0) ATRACE(18);
           const uint64_t ps2 = f2_add(f2_add(ps[0], ps[1]), f2_add(ps[2], ps[3]));
           const float psum = f2_lo(ps2) + f2_hi(ps2);
           l_run = l_run * corr + psum;
@@ -554,7 +593,7 @@ __global__ void __launch_bounds__(kThreads)
             ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, status));
             if (ok) {
               tc_fence_after();
-              const uint32_t ocol = trow + kColO;
+              const uint32_t ocol = trow + kColO + 64 * (g & 1);
 #pragma unroll 1
               for (int c = 0; c < kDh; c += 32) {
                 float o[32];
@@ -570,52 +609,26 @@ __global__ void __launch_bounds__(kThreads)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t & 1]);
         if (lane == 0) ATRACE(5);
-      }
-      // epilogue of the item: O / l -> f16 (the next P V overwrites O only
-      // after this thread's next arrival on p_full)
-      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, status));
-      if (lane == 0) ATRACE(6);
-      if (ok) {
-        tc_fence_after();
-        const float inv = 1.0f / l_run;
-        const uint32_t ocol = trow + kColO;
-        // each 32-column half of the warp's 32 rows goes through a 2 KB
-        // staging tile (16-byte chunks XOR-swizzled by row, conflict-free both
-        // ways), so every store instruction writes 8 rows x 64 contiguous bytes
-        uint8_t* stage = smem + kOffStage + qd * 2048;
-        const int rq0 = it.q0 + qd * 32;  // first query row of this warp
-#pragma unroll 1
-        for (int c = 0; c < kDh; c += 32) {
-          float o[32];
-          tmem_ld_32x32b_x32(ocol + c, o);
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w;
-            w.x = pack_f16x2_sat(o[i] * inv, o[i + 1] * inv);
-            w.y = pack_f16x2_sat(o[i + 2] * inv, o[i + 3] * inv);
-            w.z = pack_f16x2_sat(o[i + 4] * inv, o[i + 5] * inv);
-            w.w = pack_f16x2_sat(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4*>(stage + lane * 64 + 16 * ((i >> 3) ^ ((lane >> 1) & 3))) = w;
-          }
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int rr = k * 8 + (lane >> 2), ch = lane & 3;
-            const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * 64 + 16 * (ch ^ ((rr >> 1) & 3)));
-            if (rq0 + rr < L)
-              *reinterpret_cast<uint4*>(out + (row0 + rq0 + rr) * inner + it.h * kDh + c + ch * 8) = w;
-          }
-          __syncwarp();
+        if (j == 0 && has_pend) {
+          // the previous item's P V finished while this step ran; its O
+          // buffer is reused by the item after this one, whose first P this
+          // thread releases only after these reads
+          if (ok) ok = epilogue(pend);
+          has_pend = false;
+          if (lane == 0) ATRACE(7);
         }
       }
-      if (lane == 0) ATRACE(7);
+      pend = Pending{row0, it.q0, it.h, t - 1, g, 1.0f / l_run};
+      has_pend = true;
       ++g;
     }
+    if (has_pend && ok) epilogue(pend);
   }
 
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  ATRACE_NS(31);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

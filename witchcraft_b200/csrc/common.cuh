@@ -250,9 +250,12 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 // Same, saturating to the finite f16 range (+-65504) so an activation that
-// leaves the range stays finite instead of becoming inf.
+// leaves the range stays finite instead of becoming inf (one cvt.satfinite:
+// in-range values round exactly as above, larger magnitudes give +-65504).
 __device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
-  return pack_f16x2(fminf(fmaxf(lo, -65504.f), 65504.f), fminf(fmaxf(hi, -65504.f), 65504.f));
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // Packed f32x2 arithmetic (one instruction for two lanes of f32 on sm_100).
