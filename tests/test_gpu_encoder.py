@@ -96,8 +96,8 @@ def test_xtr_query_shapes(xtr_gpu, xtr_oracle):
 
 @pytest.mark.parametrize("B,L,lengths", [(1, 32, [32]), (1, 20, [13]), (2, 16, [16, 5])])
 def test_xtr_small_batch_path(xtr_gpu, xtr_oracle, B, L, lengths):
-    """B * L <= 32 tokens: the small-M layer path (input RMSNorm inside the
-    QKV / gated-FF GEMMs, residual adds inside the O / wo GEMMs)."""
+    """B * L <= 32 tokens: the small-M layer path (split-K GEMV kernels, the
+    residual add in the RMSNorm that follows, small-L attention)."""
     ids = np.random.default_rng(B * 100 + L).integers(3, 32128, (B, L)).astype(np.uint32)
     _check(xtr_gpu.forward(ids, lengths), xtr_oracle.encode(ids, lengths), lengths)
 

@@ -76,7 +76,7 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
     }
   }
   ss = warp_sum(ss);
-  const float den = sqrtf(ss / static_cast<float>(D) + eps);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
 #pragma unroll
   for (int c = 0; c < kMaxD / 256; ++c) {
     if (c < nb) {
@@ -87,10 +87,10 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
       const float4 w0 = reinterpret_cast<const float4*>(w + e)[0];
       const float4 w1 = reinterpret_cast<const float4*>(w + e)[1];
       uint4 o;
-      o.x = pack_f16x2_sat(v[c][0] / den * w0.x, v[c][1] / den * w0.y);
-      o.y = pack_f16x2_sat(v[c][2] / den * w0.z, v[c][3] / den * w0.w);
-      o.z = pack_f16x2_sat(v[c][4] / den * w1.x, v[c][5] / den * w1.y);
-      o.w = pack_f16x2_sat(v[c][6] / den * w1.z, v[c][7] / den * w1.w);
+      o.x = pack_f16x2_sat(v[c][0] * inv * w0.x, v[c][1] * inv * w0.y);
+      o.y = pack_f16x2_sat(v[c][2] * inv * w0.z, v[c][3] * inv * w0.w);
+      o.z = pack_f16x2_sat(v[c][4] * inv * w1.x, v[c][5] * inv * w1.y);
+      o.w = pack_f16x2_sat(v[c][6] * inv * w1.z, v[c][7] * inv * w1.w);
       *reinterpret_cast<uint4*>(xn + static_cast<size_t>(m) * D + e) = o;
     }
   }
@@ -127,7 +127,9 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
     }
   }
   ss = warp_sum(ss);
-  const float den = sqrtf(ss / static_cast<float>(D) + eps);
+  // x / den as x * (1 / den): one division per row instead of one per
+  // element (the product differs from the quotient by at most one f32 ulp)
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
   uint2* yr = reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * D);
   const float4* wr = reinterpret_cast<const float4*>(w);
 #pragma unroll
@@ -135,8 +137,8 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
     if (g < ng) {
       const float4 ww = wr[lane + 32 * g];
       uint2 o;
-      o.x = pack_f16x2_sat(v[g].x / den * ww.x, v[g].y / den * ww.y);
-      o.y = pack_f16x2_sat(v[g].z / den * ww.z, v[g].w / den * ww.w);
+      o.x = pack_f16x2_sat(v[g].x * inv * ww.x, v[g].y * inv * ww.y);
+      o.y = pack_f16x2_sat(v[g].z * inv * ww.z, v[g].w * inv * ww.w);
       yr[lane + 32 * g] = o;
     }
   }

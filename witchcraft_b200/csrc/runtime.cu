@@ -1073,9 +1073,36 @@ uint8_t* noalloc_scratch_ptr(int dev, cudaError_t* err) {
 
 // The launch sequence of one forward over the given activation buffers
 // (x, xn, qkv, att, hbuf) and their tensor maps.
+// Optional per-launch event marks for timeline analysis (off in the library
+// build): an event after every launch of the last forward.
+#ifdef WC_FWD_EVENTS
+cudaEvent_t g_fwd_ev[128];
+int g_fwd_n = 0;
+#define FWD_MARK()                                                          \
+  do {                                                                      \
+    if (g_fwd_n < 128) {                                                    \
+      if (!g_fwd_ev[g_fwd_n]) cudaEventCreate(&g_fwd_ev[g_fwd_n]);          \
+      cudaEventRecord(g_fwd_ev[g_fwd_n++], st);                             \
+    }                                                                       \
+  } while (0)
+#define FWD_BEGIN() \
+  do {              \
+    g_fwd_n = 0;    \
+    FWD_MARK();     \
+  } while (0)
+#else
+#define FWD_MARK() \
+  do {             \
+  } while (0)
+#define FWD_BEGIN() \
+  do {              \
+  } while (0)
+#endif
+
 int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half* hbuf, const CUtensorMap& tm_xn,
                const CUtensorMap& tm_att, const CUtensorMap& tm_h, const uint32_t* ids, const int32_t* lengths,
                int B, int L, float* out, float* norms, float* outn, cudaStream_t st) {
+  FWD_BEGIN();
   const T5Config& c = h->cfg;
   const int D = c.d_model, F = c.d_ff, I = h->inner, H = c.num_heads;
   const int M = B * L;
@@ -1092,20 +1119,28 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, x, xn, st)) !=
       cudaSuccess)
     return cuda_fail(h, e, "embedding launch");
+  FWD_MARK();
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
     if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tmh_qkv, w.tmh_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
+    FWD_MARK();
     e = attention_small_supports(L) ? attention_small_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)
                                     : attention_tc_launch(tm_qkv, att, lengths, B, L, H, h->rel_bias, h->bt,
                                                           h->d_status, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "attention launch");
+    FWD_MARK();
     if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tmh_o, w.tmh_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
+    FWD_MARK();
     if ((e = rmsnorm_launch(x, res_delta, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    FWD_MARK();
     if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tmh_wi0, w.tmh_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
+    FWD_MARK();
     if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tmh_wo, w.tmh_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo))) return rc;
+    FWD_MARK();
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(x, res_delta, next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    FWD_MARK();
   }
   return gemm(h, kEpiProj, 128, tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,
               lengths, L);
@@ -1160,3 +1195,13 @@ extern "C" int wc_selftest_wait_timeout(uint64_t limit_ns) {
     return WC_E_CUDA;  // the context did not stay usable
   return (s & kStatusWaitTimeout) ? WC_E_TIMEOUT : WC_E_CUDA;
 }
+
+#ifdef WC_FWD_EVENTS
+// Milliseconds between consecutive marks of the last forward; returns the count.
+extern "C" int wc_fwd_events(float* ms, int max) {
+  const int n = wc::g_fwd_n;
+  cudaEventSynchronize(wc::g_fwd_ev[n - 1]);
+  for (int i = 1; i < n && i <= max; ++i) cudaEventElapsedTime(&ms[i - 1], wc::g_fwd_ev[i - 1], wc::g_fwd_ev[i]);
+  return n - 1;
+}
+#endif
