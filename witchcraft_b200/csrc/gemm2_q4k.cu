@@ -59,6 +59,15 @@ constexpr int kOutBytes = 32 * 128;  // one staged 32-row x 128-byte output chun
 constexpr int kOffOut = kOffB + kSB * kBBytes;  // [epilogue warp][2] staged chunks
 constexpr int kOffBar = kOffOut + 4 * 2 * kOutBytes;
 constexpr int kSmem = 1024 + kOffBar + 512;
+// With f16 weights there is no raw Q4_K ring, and its space buys a deeper
+// X / B ring: stage i holds X and the weight rows of the same K step.
+constexpr int kSAf = 6;
+constexpr int kOffAf = 0;
+constexpr int kOffBf = kOffAf + kSAf * kABytes;
+constexpr int kOffOutF = kOffBf + kSAf * kBBytes;
+constexpr int kOffBarF = kOffOutF + 4 * 2 * kOutBytes;
+constexpr int kSmemF = 1024 + kOffBarF + 512;
+static_assert(kSmemF <= 232448 && kSmem <= 232448, "dynamic shared memory per block");
 constexpr int kEpiWarps = 4;  // one per TMEM lane quarter
 constexpr int kThreads = 64 + 256 + 32 * kEpiWarps;
 constexpr int kDequantWarps = 8;
@@ -181,13 +190,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                      GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem + kOffA;
+  constexpr int SA = WF16 ? kSAf : kSA;  // X (and f16 B) ring depth
+  uint8_t* sA = smem + (WF16 ? kOffAf : kOffA);
   uint8_t* sW = smem + kOffW;
-  uint8_t* sB = smem + kOffB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full_a = bars;                 // [kSA]  even CTA: X bytes of both CTAs
-  uint64_t* empty_a = full_a + kSA;        // [kSA]  each CTA: MMA done with the stage
-  uint64_t* full_w = empty_a + kSA;        // [kSW]  local raw Q4_K landed
+  uint8_t* sB = smem + (WF16 ? kOffBf : kOffB);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (WF16 ? kOffBarF : kOffBar));
+  uint64_t* full_a = bars;                 // [SA]   even CTA: X bytes of both CTAs
+  uint64_t* empty_a = full_a + SA;         // [SA]   each CTA: MMA done with the stage
+  uint64_t* full_w = empty_a + SA;         // [kSW]  local raw Q4_K landed
   uint64_t* empty_w = full_w + kSW;        // [kSW]  local dequant warps done with it
   uint64_t* full_b = empty_w + kSW;        // [kSB]  even CTA: the owning warp pair of both CTAs
   uint64_t* empty_b = full_b + kSB;        // [kSB]  each CTA: MMA done with the stage
@@ -208,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ncl = static_cast<int>(num_clusters());
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kSA; ++i) {
+    for (int i = 0; i < SA; ++i) {
       mbar_init(&full_a[i], 1);
       mbar_init(&empty_a[i], 1);
     }
@@ -258,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sW + sw * kWBytes, wmap, &full_w[sw], (t >> 2) * 144, w_row0);
             ++iw;
           }
-          const uint32_t sa = ia % kSA;
-          if (!(ok = mbar_wait(&empty_a[sa], ((ia / kSA) & 1) ^ 1, p.status))) break;
+          const uint32_t sa = ia % SA;
+          if (!(ok = mbar_wait(&empty_a[sa], ((ia / SA) & 1) ^ 1, p.status))) break;
           if (leader) mbar_arrive_expect_tx(&full_a[sa], WF16 ? 2 * (kABytes + kBBytes) : 2 * kABytes);
           tma_load_2d_pair(sA + sa * kABytes, &tmA, map_to_rank(&full_a[sa], 0), t * kBK, m0);
           if (WF16)  // B stage sa holds this CTA's weight rows of the same K step
@@ -280,8 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * kBN;
         for (int t = 0; t < ksteps; ++t, ++ia, ++ib) {
-          const uint32_t sa = ia % kSA, sb = ib % kSB;
-          ok = mbar_wait_cluster(&full_a[sa], (ia / kSA) & 1, p.status) &&
+          const uint32_t sa = ia % SA, sb = ib % kSB;
+          ok = mbar_wait_cluster(&full_a[sa], (ia / SA) & 1, p.status) &&
                (WF16 || mbar_wait_cluster(&full_b[sb], (ib / kSB) & 1, p.status));
           if (!ok) break;
           tc_fence_after();
@@ -351,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
-    uint8_t* sOutW = smem + kOffOut + (warp - 10) * 2 * kOutBytes;
+    uint8_t* sOutW = smem + (WF16 ? kOffOutF : kOffOut) + (warp - 10) * 2 * kOutBytes;
     uint32_t ostage = 0;
     const uint32_t acc_empty_leader0 = map_to_rank(&acc_empty[0], 0);
     uint32_t it = 0;
@@ -450,14 +460,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int EPI, bool WF16>
 cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& out,
                    const GemmParams& p, int num_sms, cudaStream_t st) {
-  static_assert(kSA == kSB, "with f16 weights the B stages follow the X stages");
+  constexpr int smem_bytes = WF16 ? kSmemF : kSmem;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm2_q4k_kernel<EPI, WF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        cudaFuncSetAttribute(gemm2_q4k_kernel<EPI, WF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
@@ -468,7 +478,7 @@ cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMa
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  return launch_pdl(gemm2_q4k_kernel<EPI, WF16>, dim3(2 * clusters), dim3(kThreads), kSmem, st, attr, 1, a, w0, w1, out, p);
+  return launch_pdl(gemm2_q4k_kernel<EPI, WF16>, dim3(2 * clusters), dim3(kThreads), smem_bytes, st, attr, 1, a, w0, w1, out, p);
 }
 
 }  // namespace
