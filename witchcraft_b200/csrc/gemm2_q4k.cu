@@ -59,15 +59,22 @@ constexpr int kOutBytes = 32 * 128;  // one staged 32-row x 128-byte output chun
 constexpr int kOffOut = kOffB + kSB * kBBytes;  // [epilogue warp][2] staged chunks
 constexpr int kOffBar = kOffOut + 4 * 2 * kOutBytes;
 constexpr int kSmem = 1024 + kOffBar + 512;
-// With f16 weights there is no raw Q4_K ring, and its space buys a deeper
-// X / B ring: stage i holds X and the weight rows of the same K step.
-constexpr int kSAf = 6;
-constexpr int kOffAf = 0;
-constexpr int kOffBf = kOffAf + kSAf * kABytes;
-constexpr int kOffOutF = kOffBf + kSAf * kBBytes;
-constexpr int kOffBarF = kOffOutF + 4 * 2 * kOutBytes;
-constexpr int kSmemF = 1024 + kOffBarF + 512;
-static_assert(kSmemF <= 232448 && kSmem <= 232448, "dynamic shared memory per block");
+// Shared-memory plan per variant.  With f16 weights there is no raw Q4_K
+// ring, and its space buys a deeper X / B ring: stage i holds X and the
+// weight rows of the same K step.  (Four staged output chunks per epilogue
+// warp instead of two, at the cost of one stage, made the f32 epilogues no
+// faster.)
+template <int EPI, bool WF16>
+struct Plan {
+  static constexpr int kStages = WF16 ? 6 : kSA;
+  static constexpr int kNOut = 2;  // staged output chunks per epilogue warp
+  static constexpr int kOffA_ = 0;
+  static constexpr int kOffB_ = WF16 ? kStages * kABytes : kOffB;
+  static constexpr int kOffOut_ = WF16 ? kOffB_ + kStages * kBBytes : kOffOut;
+  static constexpr int kOffBar_ = kOffOut_ + 4 * kNOut * kOutBytes;
+  static constexpr int kSmem_ = 1024 + kOffBar_ + 512;
+  static_assert(kSmem_ <= 232448, "dynamic shared memory per block");
+};
 constexpr int kEpiWarps = 4;  // one per TMEM lane quarter
 constexpr int kThreads = 64 + 256 + 32 * kEpiWarps;
 constexpr int kDequantWarps = 8;
@@ -190,11 +197,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                      GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int SA = WF16 ? kSAf : kSA;  // X (and f16 B) ring depth
-  uint8_t* sA = smem + (WF16 ? kOffAf : kOffA);
+  using PL = Plan<EPI, WF16>;
+  constexpr int SA = PL::kStages;  // X (and f16 B) ring depth
+  uint8_t* sA = smem + PL::kOffA_;
   uint8_t* sW = smem + kOffW;
-  uint8_t* sB = smem + (WF16 ? kOffBf : kOffB);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (WF16 ? kOffBarF : kOffBar));
+  uint8_t* sB = smem + PL::kOffB_;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PL::kOffBar_);
   uint64_t* full_a = bars;                 // [SA]   even CTA: X bytes of both CTAs
   uint64_t* empty_a = full_a + SA;         // [SA]   each CTA: MMA done with the stage
   uint64_t* full_w = empty_a + SA;         // [kSW]  local raw Q4_K landed
@@ -361,7 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
-    uint8_t* sOutW = smem + (WF16 ? kOffOutF : kOffOut) + (warp - 10) * 2 * kOutBytes;
+    constexpr int NOUT = PL::kNOut;
+    uint8_t* sOutW = smem + PL::kOffOut_ + (warp - 10) * NOUT * kOutBytes;
     uint32_t ostage = 0;
     const uint32_t acc_empty_leader0 = map_to_rank(&acc_empty[0], 0);
     uint32_t it = 0;
@@ -388,8 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int y0 = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + q * 32;
 #pragma unroll 1
         for (int c = 0; c < kOutCols; c += kCW, ++ostage) {
-          uint8_t* sbuf = sOutW + (ostage & 1) * kOutBytes;
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          uint8_t* sbuf = sOutW + (ostage % NOUT) * kOutBytes;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(NOUT - 1) : "memory");
           __syncwarp();
           uint8_t* srow = sbuf + lane * 128;
           if (kF32Out) {
@@ -460,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int EPI, bool WF16>
 cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& out,
                    const GemmParams& p, int num_sms, cudaStream_t st) {
-  constexpr int smem_bytes = WF16 ? kSmemF : kSmem;
+  constexpr int smem_bytes = Plan<EPI, WF16>::kSmem_;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
