@@ -183,3 +183,20 @@ def test_forward_many_equals_single_calls(tiny_gpu):
             ref, rn, _ = tiny_gpu.forward_full(ids, lens)
             np.testing.assert_array_equal(o, ref)
             np.testing.assert_array_equal(nr, rn)
+
+
+def test_forward_many_two_lanes(tiny_gpu):
+    """Batches past the graph size alternate between two compute streams with
+    separate activation buffers; every batch still equals its single call,
+    including a small batch on the second lane."""
+    rng = np.random.default_rng(22)
+    batches = []
+    for B, L in [(40, 128), (9, 600), (33, 160), (3, 25), (70, 64)]:
+        ids = rng.integers(3, 512, (B, L)).astype(np.uint32)
+        lens = rng.integers(1, L + 1, B).astype(np.int32)
+        batches.append((ids, lens))
+    got, gn = tiny_gpu.forward_many(batches, with_norms=True)
+    for (ids, lens), o, nr in zip(batches, got, gn):
+        ref, rn, _ = tiny_gpu.forward_full(ids, lens)
+        np.testing.assert_array_equal(o, ref)
+        np.testing.assert_array_equal(nr, rn)

@@ -170,6 +170,17 @@ struct wc_t5 {
   float *io_out[2] = {}, *io_norms[2] = {};
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t ev_in[2] = {}, ev_fwd[2] = {}, ev_out[2] = {};
+  // wc_t5_forward_many's second compute lane for large batches: odd batches
+  // run on their own stream with their own activation buffers, so one
+  // batch's memory-bound kernels (RMSNorm, attention) share the SMs with the
+  // other's GEMMs; created on first use
+  cudaStream_t lane_stream = nullptr;
+  cudaEvent_t ev_lane = nullptr;
+  uint8_t* lane_ws = nullptr;
+  int64_t lane_rows = 0;
+  float* lane_x = nullptr;
+  __half *lane_xn = nullptr, *lane_qkv = nullptr, *lane_att = nullptr, *lane_h = nullptr;
+  CUtensorMap lane_tm_xn, lane_tm_att, lane_tm_h;
   // CUDA graphs of the kernel sequence for small batches, keyed by shape,
   // buffers and stream; an entry first records that the key was seen and is
   // captured on its second use.
@@ -409,6 +420,12 @@ extern "C" int wc_t5_destroy(wc_t5* h) {
       if (h->ev_out[i]) cudaEventDestroy(h->ev_out[i]);
     }
     if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
+    if (h->lane_stream) {
+      cudaStreamSynchronize(h->lane_stream);
+      cudaStreamDestroy(h->lane_stream);
+    }
+    if (h->ev_lane) cudaEventDestroy(h->ev_lane);
+    if (h->lane_ws) cudaFree(h->lane_ws);
     if (h->d_status) cudaFree(h->d_status);
     if (h->stream) cudaStreamDestroy(h->stream);
   }
@@ -807,6 +824,46 @@ int ensure_io(wc_t5* h, int64_t rows, int B) {
   return WC_OK;
 }
 
+// Stream, event and activation buffers (x, xn, qkv, att, h) of the second
+// compute lane for batches of up to `rows` tokens.
+int ensure_lane(wc_t5* h, int64_t rows) {
+  if (!h->lane_stream) {
+    cudaError_t e = cudaStreamCreateWithFlags(&h->lane_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->ev_lane, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(h, e, "second compute lane stream / event");
+  }
+  if (rows <= h->lane_rows) return WC_OK;
+  if (h->lane_ws) {
+    cudaStreamSynchronize(h->lane_stream);
+    cudaFree(h->lane_ws);
+    h->lane_ws = nullptr;
+    h->lane_rows = 0;
+  }
+  const int64_t cap = (rows + 127) / 128 * 128;
+  const int D = h->cfg.d_model, F = h->cfg.d_ff, I = h->inner;
+  size_t off = 0;
+  const size_t o_x = off; off = align256(off + cap * D * 4);
+  const size_t o_xn = off; off = align256(off + cap * D * 2);
+  const size_t o_qkv = off; off = align256(off + cap * std::max(3 * I * 2, D * 4));
+  const size_t o_att = off; off = align256(off + cap * I * 2);
+  const size_t o_h = off; off = align256(off + cap * F * 2);
+  cudaError_t e = cudaMalloc(&h->lane_ws, off);
+  if (e != cudaSuccess) {
+    h->lane_ws = nullptr;
+    return cuda_fail(h, e, "second compute lane workspace");
+  }
+  h->lane_x = reinterpret_cast<float*>(h->lane_ws + o_x);
+  h->lane_xn = reinterpret_cast<__half*>(h->lane_ws + o_xn);
+  h->lane_qkv = reinterpret_cast<__half*>(h->lane_ws + o_qkv);
+  h->lane_att = reinterpret_cast<__half*>(h->lane_ws + o_att);
+  h->lane_h = reinterpret_cast<__half*>(h->lane_ws + o_h);
+  if (!make_act_map(&h->lane_tm_xn, h->lane_xn, cap, D) || !make_act_map(&h->lane_tm_att, h->lane_att, cap, I) ||
+      !make_act_map(&h->lane_tm_h, h->lane_h, cap, F))
+    return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a second-lane activation buffer");
+  h->lane_rows = cap;
+  return WC_OK;
+}
+
 }  // namespace
 }  // namespace wc
 
@@ -826,11 +883,22 @@ extern "C" int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, c
     max_b = std::max(max_b, B[i]);
   }
   DeviceGuard g(h->device);
+  // two compute lanes when there are several batches and the largest is
+  // past the captured-graph size
+  // (WC_FORWARD_LANES=1 keeps every batch on the handle's stream)
+  static const bool one_lane = [] {
+    const char* v = getenv("WC_FORWARD_LANES");
+    return v && v[0] == '1' && v[1] == 0;
+  }();
+  const bool two_lanes = !one_lane && n > 1 && max_rows > kGraphMaxRows;
   int rc = ensure_workspace(h, max_rows, max_b);
   if (!rc) rc = ensure_io(h, max_rows, max_b);
+  if (!rc && two_lanes) rc = ensure_lane(h, max_rows);
   if (rc) return rc;
   cudaStream_t cs = h->stream, ps = h->copy_stream;
   cudaError_t e = cudaMemsetAsync(h->d_status, 0, 4, cs);
+  if (two_lanes && e == cudaSuccess && (e = cudaEventRecord(h->ev_lane, cs)) == cudaSuccess)
+    e = cudaStreamWaitEvent(h->lane_stream, h->ev_lane, 0);  // after the status reset
   auto upload = [&](int i) -> cudaError_t {
     const int s = i & 1;
     const int64_t M = static_cast<int64_t>(B[i]) * L[i];
@@ -841,16 +909,22 @@ extern "C" int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, c
   };
   for (int i = 0; i < 2 && i < n && e == cudaSuccess; ++i) e = upload(i);
   for (int i = 0; i < n && e == cudaSuccess && rc == WC_OK; ++i) {
-    const int s = i & 1;
+    const int s = i & 1;  // I/O set, and compute lane with two lanes
     const int64_t M = static_cast<int64_t>(B[i]) * L[i];
     float* nrm = norms ? norms[i] : nullptr;
+    cudaStream_t fs = two_lanes && s ? h->lane_stream : cs;
     // compute: inputs of batch i landed; d_out of set s read out (batch i - 2)
-    if ((e = cudaStreamWaitEvent(cs, h->ev_in[s], 0)) != cudaSuccess) break;
-    if (i >= 2 && (e = cudaStreamWaitEvent(cs, h->ev_out[s], 0)) != cudaSuccess) break;
-    rc = forward_cached(h, h->io_ids[s], h->io_len[s], B[i], L[i], h->io_out[s], nrm ? h->io_norms[s] : nullptr,
-                        nullptr, cs);
+    if ((e = cudaStreamWaitEvent(fs, h->ev_in[s], 0)) != cudaSuccess) break;
+    if (i >= 2 && (e = cudaStreamWaitEvent(fs, h->ev_out[s], 0)) != cudaSuccess) break;
+    if (fs == cs)
+      rc = forward_cached(h, h->io_ids[s], h->io_len[s], B[i], L[i], h->io_out[s], nrm ? h->io_norms[s] : nullptr,
+                          nullptr, cs);
+    else
+      rc = forward_on(h, h->lane_x, h->lane_xn, h->lane_qkv, h->lane_att, h->lane_h, h->lane_tm_xn,
+                      h->lane_tm_att, h->lane_tm_h, h->io_ids[s], h->io_len[s], B[i], L[i], h->io_out[s],
+                      nrm ? h->io_norms[s] : nullptr, nullptr, fs);
     if (rc) break;
-    if ((e = cudaEventRecord(h->ev_fwd[s], cs)) != cudaSuccess) break;
+    if ((e = cudaEventRecord(h->ev_fwd[s], fs)) != cudaSuccess) break;
     // copy: results of batch i out, then inputs of batch i + 2 into set s
     if ((e = cudaStreamWaitEvent(ps, h->ev_fwd[s], 0)) != cudaSuccess) break;
     if ((e = cudaMemcpyAsync(out[i], h->io_out[s], M * h->d_proj * 4, cudaMemcpyDeviceToHost, ps)) != cudaSuccess)
@@ -859,7 +933,11 @@ extern "C" int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, c
     if ((e = cudaEventRecord(h->ev_out[s], ps)) != cudaSuccess) break;
     if (i + 2 < n && (e = upload(i + 2)) != cudaSuccess) break;
   }
-  const cudaError_t es = cudaStreamSynchronize(ps);
+  cudaError_t es = cudaStreamSynchronize(ps);
+  if (two_lanes) {
+    const cudaError_t el = cudaStreamSynchronize(h->lane_stream);
+    if (es == cudaSuccess) es = el;
+  }
   if (rc) {
     cudaStreamSynchronize(cs);
     return rc;
