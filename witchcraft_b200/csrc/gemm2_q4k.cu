@@ -56,9 +56,7 @@ constexpr int kOffA = 0;
 constexpr int kOffW = kOffA + kSA * kABytes;
 constexpr int kOffB = kOffW + kSW * kWBytes;
 constexpr int kOutBytes = 32 * 128;  // one staged 32-row x 128-byte output chunk
-constexpr int kOffOut = kOffB + kSB * kBBytes;  // [epilogue warp][2] staged chunks
-constexpr int kOffBar = kOffOut + 4 * 2 * kOutBytes;
-constexpr int kSmem = 1024 + kOffBar + 512;
+constexpr int kOffOut = kOffB + kSB * kBBytes;  // [epilogue warp][2] staged chunks (Q4_K variant)
 // Shared-memory plan per variant.  With f16 weights there is no raw Q4_K
 // ring, and its space buys a deeper X / B ring: stage i holds X and the
 // weight rows of the same K step.  (Four staged output chunks per epilogue
@@ -190,6 +188,15 @@ __device__ __forceinline__ uint4 dequant8_f16(uint32_t x0, uint32_t x1, uint64_t
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Optional wait accounting for pipeline analysis (off in the library build):
+// per CTA, cycles the MMA thread waited for accumulators / operand stages and
+// its loop total, the producer's waits for free stages, the first epilogue
+// warp's waits for accumulators.
+#ifdef WC_GEMM_TRACE
+__device__ unsigned long long g_gemm_trace[512][8];
+#define GT_NOW() static_cast<unsigned long long>(clock64())
+#endif
+
 template <int EPI, bool WF16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_q4k_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
@@ -277,7 +284,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++iw;
           }
           const uint32_t sa = ia % SA;
+#ifdef WC_GEMM_TRACE
+          const unsigned long long w0_ = GT_NOW();
+#endif
           if (!(ok = mbar_wait(&empty_a[sa], ((ia / SA) & 1) ^ 1, p.status))) break;
+#ifdef WC_GEMM_TRACE
+          g_gemm_trace[blockIdx.x][4] += GT_NOW() - w0_;
+#endif
           if (leader) mbar_arrive_expect_tx(&full_a[sa], WF16 ? 2 * (kABytes + kBBytes) : 2 * kABytes);
           tma_load_2d_pair(sA + sa * kABytes, &tmA, map_to_rank(&full_a[sa], 0), t * kBK, m0);
           if (WF16)  // B stage sa holds this CTA's weight rows of the same K step
@@ -292,16 +305,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN);
       uint32_t ia = 0, ib = 0, it = 0;
       bool ok = true;
+#ifdef WC_GEMM_TRACE
+      const unsigned long long t0_ = GT_NOW();
+      unsigned long long wacc_ = 0, wfull_ = 0, nk_ = 0;
+#endif
       for (int tile = cid; tile < n_total && ok; tile += ncl, ++it) {
         const uint32_t buf = it & 1;
+#ifdef WC_GEMM_TRACE
+        const unsigned long long w0_ = GT_NOW();
+#endif
         if (!(ok = mbar_wait_cluster(&acc_empty[buf], ((it >> 1) & 1) ^ 1, p.status))) break;
+#ifdef WC_GEMM_TRACE
+        wacc_ += GT_NOW() - w0_;
+#endif
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * kBN;
         for (int t = 0; t < ksteps; ++t, ++ia, ++ib) {
           const uint32_t sa = ia % SA, sb = ib % kSB;
+#ifdef WC_GEMM_TRACE
+          const unsigned long long w1_ = GT_NOW();
+#endif
           ok = mbar_wait_cluster(&full_a[sa], (ia / SA) & 1, p.status) &&
                (WF16 || mbar_wait_cluster(&full_b[sb], (ib / kSB) & 1, p.status));
           if (!ok) break;
+#ifdef WC_GEMM_TRACE
+          wfull_ += GT_NOW() - w1_;
+          ++nk_;
+#endif
           tc_fence_after();
           const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + sa * kABytes));
           const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + (WF16 ? sa : sb) * kBBytes));
@@ -313,6 +343,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) tc_commit_pair(&acc_full[buf]);
       }
+#ifdef WC_GEMM_TRACE
+      g_gemm_trace[blockIdx.x][0] = wacc_;
+      g_gemm_trace[blockIdx.x][1] = wfull_;
+      g_gemm_trace[blockIdx.x][2] = GT_NOW() - t0_;
+      g_gemm_trace[blockIdx.x][3] = nk_;
+#endif
     }
   } else if (warp < 2 + kDequantWarps) {
     if (WF16) {
@@ -368,7 +404,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;
     constexpr int NOUT = PL::kNOut;
     uint8_t* sOutW = smem + PL::kOffOut_ + (warp - 10) * NOUT * kOutBytes;
     uint32_t ostage = 0;
@@ -376,10 +411,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;
     for (int tile = cid; tile < n_total; tile += ncl, ++it) {
       const uint32_t buf = it & 1;
+#ifdef WC_GEMM_TRACE
+      const unsigned long long w0_ = GT_NOW();
+#endif
       const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], (it >> 1) & 1, p.status));
       if (!ok) break;
+#ifdef WC_GEMM_TRACE
+      if (warp == 10 && lane == 0) g_gemm_trace[blockIdx.x][6] += GT_NOW() - w0_;
+#endif
       tc_fence_after();
-      const int m = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + row;
       const int nt = tile % n_tiles;
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
       {
@@ -491,6 +531,18 @@ cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMa
 }
 
 }  // namespace
+
+#ifdef WC_GEMM_TRACE
+extern "C" int wc_gemm_trace(unsigned long long* host, int reset) {
+  if (reset) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_gemm_trace);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(g_gemm_trace));
+    return static_cast<int>(e);
+  }
+  return static_cast<int>(cudaMemcpyFromSymbol(host, g_gemm_trace, sizeof(g_gemm_trace)));
+}
+#endif
 
 bool gemm2_q4k_supports(int epi, int M, int N, int K) {
   return (epi == kEpiF16 || epi == kEpiGeGLU || epi == kEpiResid || epi == kEpiF32) && M >= 1 && N % kBN == 0 &&
