@@ -12,13 +12,41 @@
 
 #include <utility>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 namespace wc {
+
+// Asks once per (device, kernel) for the largest shared-memory carveout, so
+// that consecutive kernels of the forward, whatever shared memory each uses,
+// run under one SM configuration and the next one can start on an SM before
+// the previous one has drained (programmatic dependent launch).
+// WC_DEFAULT_CARVEOUT=1 leaves the driver's choice.
+inline cudaError_t ensure_max_carveout(const void* func) {
+  static const bool on = [] {
+    const char* e = getenv("WC_DEFAULT_CARVEOUT");
+    return !(e && e[0] == '1');
+  }();
+  if (!on) return cudaSuccess;
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({dev, func})) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) done.insert({dev, func});
+  return e;
+}
 
 // Launches kernel on `st` with programmatic stream serialisation (see
 // pdl_wait); extra launch attributes (e.g. a cluster shape) may be appended.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                               const cudaLaunchAttribute* extra, int n_extra, Args&&... args) {
+  if (cudaError_t ce = ensure_max_carveout(reinterpret_cast<const void*>(kernel)); ce != cudaSuccess) return ce;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
