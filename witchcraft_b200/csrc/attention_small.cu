@@ -4,8 +4,10 @@
 // softmax, P.V) with warp-level mma.sync instead of the tcgen05 pipeline.
 // At L <= 64 a 128-query tcgen05 tile is mostly padding and the kernel is
 // bound by its per-step handshake latency; here one CTA owns one (sequence,
-// head), four warps each take 16 queries, and everything after the loads
-// stays in registers.
+// head), each warp takes 16 queries, and everything after the loads stays in
+// registers.  The padded tile is KL = 32 or 64 rows (L <= 32 takes the
+// smaller one: half the shared memory and warps per CTA, so twice as many
+// CTAs keep their loads in flight on an SM).
 //
 // Per CTA: Q, K, V of the head (rows past L zero) in padded shared memory
 // (144-byte rows: conflict-free ldmatrix), the head's bias for every
@@ -62,14 +64,16 @@ __device__ __forceinline__ int bucket_of(const BucketThresholds& bt, int delta) 
   return f + (delta > 0 ? bt.half : 0);
 }
 
-__global__ void __launch_bounds__(128)
+template <int KL>
+__global__ void __launch_bounds__(KL * 2)
     attention_small_kernel(const __half* __restrict__ qkv, __half* __restrict__ out,
                            const int32_t* __restrict__ lengths, int L, int H, const float* __restrict__ bias_tab,
                            BucketThresholds bt) {
-  __shared__ __align__(16) uint8_t sQ[kL * kRowB];
-  __shared__ __align__(16) uint8_t sK[kL * kRowB];
-  __shared__ __align__(16) uint8_t sV[kL * kRowB];
-  __shared__ float sBias[2 * kL];  // bias(key - query = delta) at delta + kL - 1, * log2(e)
+  constexpr int kT = KL * 2;  // threads: one warp per 16 queries
+  __shared__ __align__(16) uint8_t sQ[KL * kRowB];
+  __shared__ __align__(16) uint8_t sK[KL * kRowB];
+  __shared__ __align__(16) uint8_t sV[KL * kRowB];
+  __shared__ float sBias[2 * KL];  // bias(key - query = delta) at delta + KL - 1, * log2(e)
   __shared__ float sCol[64];       // this head's column of the bias table
   pdl_wait();
   pdl_launch_next();
@@ -79,7 +83,7 @@ __global__ void __launch_bounds__(128)
   const int inner = H * kDh;
   const size_t row0 = static_cast<size_t>(b) * L;
   if (len == 0) {
-    for (int i = tid; i < L * (kDh / 8); i += 128) {
+    for (int i = tid; i < L * (kDh / 8); i += kT) {
       const int r = i >> 3, c = i & 7;
       *reinterpret_cast<uint4*>(out + (row0 + r) * inner + h * kDh + c * 8) = make_uint4(0, 0, 0, 0);
     }
@@ -87,25 +91,26 @@ __global__ void __launch_bounds__(128)
   }
   // all loads in flight at once: Q, K, V rows (past L zero-filled) by cp.async
 #pragma unroll
-  for (int k = 0; k < 3 * kL * 8 / 128; ++k) {
-    const int i = tid + 128 * k;
-    const int mat = i / (kL * 8), rem = i % (kL * 8), r = rem >> 3, c = rem & 7;
+  for (int k = 0; k < 3 * KL * 8 / kT; ++k) {
+    const int i = tid + kT * k;
+    const int mat = i / (KL * 8), rem = i % (KL * 8), r = rem >> 3, c = rem & 7;
     const uint32_t dst = smem_u32(mat == 0 ? sQ : mat == 1 ? sK : sV) + r * kRowB + c * 16;
     cp16s(dst, qkv + (row0 + (r < L ? r : 0)) * (3 * inner) + mat * inner + h * kDh + c * 8, r < L);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   if (tid < 2 * bt.half) sCol[tid] = bias_tab[tid * H + h] * 1.4426950408889634f;
   __syncthreads();
-  for (int i = tid; i < 2 * kL - 1; i += 128) sBias[i] = sCol[bucket_of(bt, i - (kL - 1))];
+  for (int i = tid; i < 2 * KL - 1; i += kT) sBias[i] = sCol[bucket_of(bt, i - (KL - 1))];
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   const int q0 = warp * 16;
   if (q0 >= L) return;
   const int g = lane >> 2, t4 = lane & 3;
-  // ---- S = Q K^T over 64 keys (8 n-blocks of 8, 4 k-steps of 16)
-  float s[8][4];
+  // ---- S = Q K^T over KL keys (KL / 8 n-blocks of 8, 4 k-steps of 16)
+  constexpr int NB = KL / 8;
+  float s[NB][4];
 #pragma unroll
-  for (int nb = 0; nb < 8; ++nb)
+  for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
     for (int i = 0; i < 4; ++i) s[nb][i] = 0.0f;
   const uint32_t qa = smem_u32(sQ) + (q0 + (lane & 15)) * kRowB + (lane >> 4) * 16;
@@ -114,7 +119,7 @@ __global__ void __launch_bounds__(128)
     uint32_t a0, a1, a2, a3;
     ldsm_x4(qa + ks * 32, a0, a1, a2, a3);
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
+    for (int nb = 0; nb < NB; ++nb) {
       uint32_t b0, b1;
       ldsm_x2(smem_u32(sK) + (nb * 8 + (lane & 7)) * kRowB + ks * 32 + ((lane >> 3) & 1) * 16, b0, b1);
       mma16816(s[nb], a0, a1, a2, a3, b0, b1);
@@ -123,11 +128,11 @@ __global__ void __launch_bounds__(128)
   // ---- v = S log2(e) + bias, mask, row max / sum (rows g and g + 8 of the block)
   float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-  for (int nb = 0; nb < 8; ++nb)
+  for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int row = q0 + g + 8 * (i >> 1), key = nb * 8 + 2 * t4 + (i & 1);
-      const float v = key < len ? fmaf(s[nb][i], 1.4426950408889634f, sBias[key - row + kL - 1]) : -INFINITY;
+      const float v = key < len ? fmaf(s[nb][i], 1.4426950408889634f, sBias[key - row + KL - 1]) : -INFINITY;
       s[nb][i] = v;
       mx[i >> 1] = fmaxf(mx[i >> 1], v);
     }
@@ -137,9 +142,9 @@ __global__ void __launch_bounds__(128)
     mx[hlf] = fmaxf(mx[hlf], __shfl_xor_sync(0xFFFFFFFFu, mx[hlf], 2));
   }
   float sum[2] = {0.0f, 0.0f};
-  uint32_t pa[4][4];  // A fragments of P for the 4 key steps
+  uint32_t pa[KL / 16][4];  // A fragments of P for the KL / 16 key steps
 #pragma unroll
-  for (int nb = 0; nb < 8; ++nb) {
+  for (int nb = 0; nb < NB; ++nb) {
     const float p0 = ex2s(s[nb][0] - mx[0]), p1 = ex2s(s[nb][1] - mx[0]);
     const float p2 = ex2s(s[nb][2] - mx[1]), p3 = ex2s(s[nb][3] - mx[1]);
     sum[0] += p0 + p1;
@@ -159,7 +164,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[nb][i] = 0.0f;
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
+  for (int ks = 0; ks < KL / 16; ++ks) {
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
       uint32_t b0, b1;
@@ -189,7 +194,10 @@ cudaError_t attention_small_launch(const __half* qkv, __half* out, const int32_t
                                    const float* bias_tab, const BucketThresholds& bt, cudaStream_t st) {
   if (B <= 0) return cudaSuccess;
   if (!attention_small_supports(L) || H <= 0 || H > 65535 || B > 65535) return cudaErrorInvalidValue;
-  return launch_pdl(attention_small_kernel, dim3(H, B), dim3(128), 0, st, nullptr, 0, qkv, out, lengths, L, H,
+  if (L <= 32)
+    return launch_pdl(attention_small_kernel<32>, dim3(H, B), dim3(64), 0, st, nullptr, 0, qkv, out, lengths, L, H,
+                      bias_tab, bt);
+  return launch_pdl(attention_small_kernel<64>, dim3(H, B), dim3(128), 0, st, nullptr, 0, qkv, out, lengths, L, H,
                     bias_tab, bt);
 }
 
