@@ -4,7 +4,7 @@
 //
 // assign_kernel: X [m][dim] f32 against C [k][dim] f32, dim <= 128.  One CTA
 //   owns 128 rows, keeps them transposed in shared memory and streams the
-//   centers through in tiles of 128; each thread holds an 8 x 8 block of dot
+//   centers through in tiles of 256; each thread holds an 8 x 16 block of dot
 //   products, each one fused-multiply-add chain over the dimensions in order
 //   (so every similarity is the same f32 number a serial fmaf loop gives), and
 //   folds each tile into its rows' running (best value, first index).  This is
@@ -29,15 +29,21 @@ namespace wc {
 
 namespace {
 
-constexpr int kTile = 128;   // rows per CTA, centers per tile
+constexpr int kTile = 128;   // rows per CTA
+constexpr int kCTile = 256;  // centers per streamed tile
 constexpr int kMaxDim = 128;
 
-__global__ void __launch_bounds__(256)
+// 256 threads: thread (ty = tid / 16, tx = tid % 16) owns rows 8 ty .. 8 ty + 7
+// and centers 64 q + 4 tx + (0..3), q = 0..3, of each tile: 128 dot products
+// per thread.  Shared-memory loads cost one wavefront per float a thread
+// reads per dimension, so the 8 x 16 block needs 24 wavefronts per 128 FMAs
+// of a warp and the FMA pipes, not the shared-memory pipe, set the pace.
+__global__ void __launch_bounds__(256, 1)
     assign_kernel(const float* __restrict__ X, int64_t m, const float* __restrict__ C, int64_t k, int dim,
                   uint32_t* __restrict__ idx) {
   extern __shared__ __align__(16) float smem[];
-  float* Xs = smem;                 // [dim][kTile] rows transposed
-  float* Cs = smem + kMaxDim * kTile;  // [dim][kTile] centers transposed
+  float* Xs = smem;                    // [dim][kTile] rows transposed
+  float* Cs = smem + kMaxDim * kTile;  // [dim][kCTile] centers transposed
   __shared__ float s_best[kTile];
   __shared__ uint32_t s_bidx[kTile];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -58,48 +64,54 @@ __global__ void __launch_bounds__(256)
     s_best[tid] = -INFINITY;
     s_bidx[tid] = 0;
   }
-  for (int64_t c0 = 0; c0 < k; c0 += kTile) {
+  for (int64_t c0 = 0; c0 < k; c0 += kCTile) {
     __syncthreads();  // previous tile consumed
-    for (int i = tid; i < kTile * d4n; i += 256) {
-      const int r = i % kTile, d4 = i / kTile;
+    for (int i = tid; i < kCTile * d4n; i += 256) {
+      const int r = i % kCTile, d4 = i / kCTile;
       const float4 v = c0 + r < k ? *reinterpret_cast<const float4*>(C + (c0 + r) * dim + 4 * d4)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-      Cs[(4 * d4) * kTile + r] = v.x;
-      Cs[(4 * d4 + 1) * kTile + r] = v.y;
-      Cs[(4 * d4 + 2) * kTile + r] = v.z;
-      Cs[(4 * d4 + 3) * kTile + r] = v.w;
+      Cs[(4 * d4) * kCTile + r] = v.x;
+      Cs[(4 * d4 + 1) * kCTile + r] = v.y;
+      Cs[(4 * d4 + 2) * kCTile + r] = v.z;
+      Cs[(4 * d4 + 3) * kCTile + r] = v.w;
     }
     __syncthreads();
-    float acc[8][8];
+    float acc[8][16];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-#pragma unroll 4
+      for (int j = 0; j < 16; ++j) acc[i][j] = 0.0f;
+#pragma unroll 2
     for (int d = 0; d < dim; ++d) {
+      // rows: 2 distinct addresses per warp (broadcast); centers: each
+      // quarter of a warp reads one contiguous 128-byte span per load
       const float4 xa = *reinterpret_cast<const float4*>(Xs + d * kTile + 8 * ty);
       const float4 xb = *reinterpret_cast<const float4*>(Xs + d * kTile + 8 * ty + 4);
-      // centers 4 tx + (0..3) and 64 + 4 tx + (0..3): each half-warp reads
-      // two contiguous 256-byte spans (no bank conflicts)
-      const float4 ca = *reinterpret_cast<const float4*>(Cs + d * kTile + 4 * tx);
-      const float4 cb = *reinterpret_cast<const float4*>(Cs + d * kTile + 64 + 4 * tx);
+      float cv[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 c4 = *reinterpret_cast<const float4*>(Cs + d * kCTile + 64 * q + 4 * tx);
+        cv[4 * q] = c4.x;
+        cv[4 * q + 1] = c4.y;
+        cv[4 * q + 2] = c4.z;
+        cv[4 * q + 3] = c4.w;
+      }
       const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-      const float cv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xv[i], cv[j], acc[i][j]);
+        for (int j = 0; j < 16; ++j) acc[i][j] = __fmaf_rn(xv[i], cv[j], acc[i][j]);
     }
-    // per row: first maximum over this thread's 8 centers, then over the 16
-    // threads of the row group (lanes tx = 0..15 of one half-warp), then fold
-    // into the running best (earlier tiles win ties)
+    // per row: first maximum over this thread's 16 centers, then over the 16
+    // threads of the row group (lanes with the same ty), then fold into the
+    // running best (earlier tiles win ties)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float bv = -INFINITY;
       uint32_t bj = 0xFFFFFFFFu;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t c = c0 + 4 * tx + 64 * (j >> 2) + (j & 3);  // increasing in j
+      for (int j = 0; j < 16; ++j) {
+        const int64_t c = c0 + 64 * (j >> 2) + 4 * tx + (j & 3);  // increasing in j
         if (c < k && (acc[i][j] > bv || bj == 0xFFFFFFFFu)) {
           bv = acc[i][j];
           bj = static_cast<uint32_t>(c);
@@ -228,7 +240,7 @@ extern "C" int wc_assign_centers(const float* d_x, int64_t m, const float* d_cen
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int smem = 2 * kMaxDim * kTile * sizeof(float);
+  const int smem = kMaxDim * (kTile + kCTile) * sizeof(float);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
     if (cudaFuncSetAttribute(assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return ifail(WC_E_CUDA, "assign kernel attribute");
