@@ -1,8 +1,8 @@
 // Device body of the short-sequence encoder attention (attention_small.cu):
 // one (sequence, head) item for padded L <= KL rows, KL = 32 or 64, by a CTA
 // of at least 2 KL threads (one warp per 16 queries; extra warps only help
-// with the loads).  Shared by the stand-alone kernel and the persistent
-// small-batch forward (small_forward.cu).
+// with the loads), as a device function; the stand-alone kernel runs one
+// item per CTA.
 #pragma once
 #include "attention.h"
 #include "common.cuh"

@@ -3,6 +3,7 @@
 // f32 statistics, no mean subtraction, no bias, x / sqrt(var + eps) * w).
 // One warp per row, 16-byte vector accesses, the row kept in registers.
 #include "common.cuh"
+#include "rownorm.cuh"
 #include "elementwise.h"
 #include "q4k.cuh"
 
@@ -96,9 +97,9 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
   }
 }
 
-// lane owns float4 groups lane + 32*i, i < D/128.  With delta != null the
-// residual add of the preceding sub-layer happens here first: x += delta
-// (written back), then the norm of the updated row.
+// One warp per row (rownorm.cuh).  With delta != null the residual add of the
+// preceding sub-layer happens here first: x += delta (written back), then the
+// norm of the updated row.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                __half* __restrict__ y, int M, int D, float eps) {
   pdl_wait();
@@ -106,42 +107,8 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
-  const int ng = D / 128;
-  float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(m) * D);
-  const float4* dr = delta ? reinterpret_cast<const float4*>(delta + static_cast<size_t>(m) * D) : nullptr;
-  float4 v[kMaxD / 128];
-  float ss = 0.f;
-#pragma unroll
-  for (int g = 0; g < kMaxD / 128; ++g) {
-    if (g < ng) {
-      v[g] = xr[lane + 32 * g];
-      if (dr) {
-        const float4 d = dr[lane + 32 * g];
-        v[g].x += d.x;
-        v[g].y += d.y;
-        v[g].z += d.z;
-        v[g].w += d.w;
-        xr[lane + 32 * g] = v[g];
-      }
-      ss += v[g].x * v[g].x + v[g].y * v[g].y + v[g].z * v[g].z + v[g].w * v[g].w;
-    }
-  }
-  ss = warp_sum(ss);
-  // x / den as x * (1 / den): one division per row instead of one per
-  // element (the product differs from the quotient by at most one f32 ulp)
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-  uint2* yr = reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * D);
-  const float4* wr = reinterpret_cast<const float4*>(w);
-#pragma unroll
-  for (int g = 0; g < kMaxD / 128; ++g) {
-    if (g < ng) {
-      const float4 ww = wr[lane + 32 * g];
-      uint2 o;
-      o.x = pack_f16x2_sat(v[g].x * inv * ww.x, v[g].y * inv * ww.y);
-      o.y = pack_f16x2_sat(v[g].z * inv * ww.z, v[g].w * inv * ww.w);
-      yr[lane + 32 * g] = o;
-    }
-  }
+  rownorm_row(x + static_cast<size_t>(m) * D, delta ? delta + static_cast<size_t>(m) * D : nullptr, true, w,
+              y + static_cast<size_t>(m) * D, D, eps, lane);
 }
 
 // A wait on an mbarrier that nothing ever arrives on, bounded by limit_ns:

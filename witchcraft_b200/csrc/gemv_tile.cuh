@@ -1,6 +1,5 @@
-// Device-side pieces of the small-M Q4_K GEMM, shared by the stand-alone
-// kernel (gemv_q4k.cu) and the persistent small-batch forward
-// (small_forward.cu).
+// Device-side pieces of the small-M Q4_K GEMM (gemv_q4k.cu), as device
+// functions a kernel can call per 16-row tile.
 //
 // One tile = 16 weight rows (output features; for the gated GELU 16 wi_0 rows
 // and the same 16 wi_1 rows) x all M <= 8 MT tokens.  The CTA's 4 warps split

@@ -1,0 +1,61 @@
+// One T5 RMSNorm row by one warp (src/quantized_t5.rs:162-173): the body of
+// the RMSNorm kernel (elementwise.cu), as a device function other kernels can
+// call and get the same bits.
+#pragma once
+#include "common.cuh"
+
+namespace wc {
+
+constexpr int kRowNormMaxD = 1024;  // d_model supported (D % 128 == 0)
+
+__device__ __forceinline__ float rownorm_warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// Lane owns float4 groups lane + 32 g, g < D / 128.  v = x (+ delta), written
+// back to x when write_x; y = f16(v * (1 / sqrt(mean(v^2) + eps)) * w).  y may
+// point to global or shared memory (8-byte aligned row).
+__device__ __forceinline__ void rownorm_row(float* __restrict__ x, const float* __restrict__ delta, bool write_x,
+                                            const float* __restrict__ w, __half* __restrict__ y, int D, float eps,
+                                            int lane) {
+  const int ng = D / 128;
+  float4* xr = reinterpret_cast<float4*>(x);
+  const float4* dr = reinterpret_cast<const float4*>(delta);
+  float4 v[kRowNormMaxD / 128];
+  float ss = 0.f;
+#pragma unroll
+  for (int g = 0; g < kRowNormMaxD / 128; ++g) {
+    if (g < ng) {
+      v[g] = xr[lane + 32 * g];
+      if (dr) {
+        const float4 d = dr[lane + 32 * g];
+        v[g].x += d.x;
+        v[g].y += d.y;
+        v[g].z += d.z;
+        v[g].w += d.w;
+        if (write_x) xr[lane + 32 * g] = v[g];
+      }
+      ss += v[g].x * v[g].x + v[g].y * v[g].y + v[g].z * v[g].z + v[g].w * v[g].w;
+    }
+  }
+  ss = rownorm_warp_sum(ss);
+  // x / den as x * (1 / den): one division per row instead of one per
+  // element (the product differs from the quotient by at most one f32 ulp)
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+  uint2* yr = reinterpret_cast<uint2*>(y);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int g = 0; g < kRowNormMaxD / 128; ++g) {
+    if (g < ng) {
+      const float4 ww = wr[lane + 32 * g];
+      uint2 o;
+      o.x = pack_f16x2_sat(v[g].x * inv * ww.x, v[g].y * inv * ww.y);
+      o.y = pack_f16x2_sat(v[g].z * inv * ww.z, v[g].w * inv * ww.w);
+      yr[lane + 32 * g] = o;
+    }
+  }
+}
+
+}  // namespace wc
