@@ -63,25 +63,37 @@ class ClockSampler:
         self._t = None
 
     def start(self):
+        # one nvidia-smi process sampling every 100 ms (-lms), read line by
+        # line, so a short timed region still gets several samples
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self._p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                        "--format=csv,noheader,nounits", "-lms", "100"],
+                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self._p = None
+            return self
+
         def run():
-            q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-            while not self._stop.is_set():
-                try:
-                    r = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                        "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                    vals = [v.strip() for v in r.stdout.strip().split(",")]
-                    if len(vals) == 6:
-                        self.rows.append(vals)
-                except Exception:
-                    pass
-                self._stop.wait(0.2)
+            for line in self._p.stdout:
+                if self._stop.is_set():
+                    break
+                vals = [v.strip() for v in line.strip().split(",")]
+                if len(vals) == 6:
+                    self.rows.append(vals)
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
         return self
 
     def stop(self):
         self._stop.set()
+        if getattr(self, "_p", None) is not None:
+            self._p.terminate()  # the sampler process this object started
+            try:
+                self._p.wait(timeout=5)
+            except Exception:
+                self._p.kill()
         if self._t:
             self._t.join(timeout=10)
         if not self.rows:
