@@ -287,11 +287,11 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars;                        // [2] per Q buffer
   uint64_t* q_empty = bars + 2;                   // [2] the item's last S is done
+  // K / V stage t % 2 is free again once S(t) / P(t) V(t) is done, which
+  // s_full / o_done of that step report (no separate empty barriers)
   uint64_t* k_full = bars + 4;                    // [kKVStages]
-  uint64_t* k_empty = k_full + kKVStages;         // [kKVStages]  freed when S(t) is done
-  uint64_t* v_full = k_empty + kKVStages;         // [kKVStages]
-  uint64_t* v_empty = v_full + kKVStages;         // [kKVStages]  freed when P(t) V(t) is done
-  uint64_t* s_full = v_empty + kKVStages;         // [2] per S buffer
+  uint64_t* v_full = k_full + kKVStages;          // [kKVStages]
+  uint64_t* s_full = v_full + kKVStages;          // [2] per S buffer
   // [2] by step parity (4 softmax warps arrive): the warps do not step in
   // lockstep, one may arrive for step t + 1 before another for step t, but
   // never for t + 2 (S(t + 2) is issued only after P(t))
@@ -318,9 +318,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kKVStages; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
@@ -374,11 +372,15 @@ __global__ void __launch_bounds__(kThreads)
         const int s = t % kKVStages;
         const uint32_t par = ((t / kKVStages) & 1) ^ 1;
         const int krow = c.it.b * L + c.j * kKeys;
-        if (!(ok = mbar_wait(&k_empty[s], par, status))) break;
+        // stage s last held K(t - 2), free once S(t - 2) is done: s_full of
+        // that step (2 stages and 2 S buffers, so the same index and parity)
+        static_assert(kKVStages == 2, "K / V stages are freed through the per-step S / P V barriers");
+        if (!(ok = mbar_wait(&s_full[s], par, status))) break;
         ATRACE(20);
         mbar_arrive_expect_tx(&k_full[s], kKVBytes);
         tma_load_2d(sK + s * kKVBytes, &tmQKV, &k_full[s], inner + c.it.h * kDh, krow);
-        if (!(ok = mbar_wait(&v_empty[s], par, status))) break;
+        // and V(t - 2), free once P(t - 2) V(t - 2) is done
+        if (!(ok = mbar_wait(&o_done[s], par, status))) break;
         ATRACE(21);
         mbar_arrive_expect_tx(&v_full[s], kKVBytes);
         tma_load_2d(sV + s * kKVBytes, &tmQKV, &v_full[s], 2 * inner + c.it.h * kDh, krow);
@@ -408,7 +410,6 @@ __global__ void __launch_bounds__(kThreads)
         ATRACE(16);
         tc_commit(&s_full[ts & 1]);
         ATRACE(12);
-        tc_commit(&k_empty[s]);
         if (cs.j == cs.it.n_kt - 1) tc_commit(&q_empty[cs.g & 1]);
         cs.advance(il);
         ++ts;
@@ -433,7 +434,6 @@ __global__ void __launch_bounds__(kThreads)
         ATRACE(14);
         tc_commit(&o_done[t & 1]);
         ATRACE(11);
-        tc_commit(&v_empty[s]);
         cp.advance(il);
         if (cs.valid(il)) ok = issue_s();  // S buffer t % 2 is free again
       }
