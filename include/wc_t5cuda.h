@@ -100,6 +100,20 @@ int wc_t5_forward_device(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengt
 int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, const int32_t* const* lengths, const int* B,
                        const int* L, float* const* out, float* const* norms);
 
+/* n device-resident batches (d_ids[i], d_lengths[i], B[i], L[i], d_out[i],
+ * d_norms[i] as in wc_t5_forward_device; d_norms may be NULL) enqueued in one
+ * call, ordered after the caller's earlier work on `stream`.  With several
+ * batches past the captured-graph size the odd batches run on the handle's
+ * second compute lane (its own stream and activation buffers), and `stream`
+ * waits for that lane before this call returns, so work the caller enqueues
+ * on `stream` afterwards (an event, a copy) sees every result.  Returns
+ * without synchronising; check with wc_t5_sync.  No reference counterpart:
+ * the entry for a caller whose batches are already on the device (a
+ * multi-GPU worker, or a pipeline that tokenises on the GPU). */
+int wc_t5_forward_many_device(wc_t5* h, int n, const uint32_t* const* d_ids, const int32_t* const* d_lengths,
+                              const int* B, const int* L, float* const* d_out, float* const* d_norms,
+                              void* stream);
+
 /* Same computation as wc_t5_forward_device, for callers that must not
  * allocate GPU memory during a call: a real-time query path that cannot
  * afford cudaMalloc's implicit device synchronisation, or a host that owns
@@ -112,7 +126,9 @@ int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, const int32_
  * looks up the array's device address (and loads the module there), so make
  * it before any stream capture.  All calls on a device share the array and
  * the handle's status word: calls that overlap on the GPU race, so serialise
- * them (one stream, or wait between calls).  Errors are reported like
+ * them (one stream, or wait between calls).  If the device is reset
+ * (cudaDeviceReset) the handle is gone with it; the array's address is looked
+ * up again in the new context by the next call.  Errors are reported like
  * wc_t5_forward_device (check with wc_t5_sync). */
 int wc_t5_forward_device_noalloc(wc_t5* h, const uint32_t* d_ids, const int32_t* d_lengths, int B, int L,
                                  float* d_out, float* d_norms, float* d_out_normalised, void* stream);

@@ -200,3 +200,85 @@ def test_forward_many_two_lanes(tiny_gpu):
         ref, rn, _ = tiny_gpu.forward_full(ids, lens)
         np.testing.assert_array_equal(o, ref)
         np.testing.assert_array_equal(nr, rn)
+
+
+def _check_rows(got, ids, lens, rows, oracle):
+    """Rows `rows` of a padded batch against the oracle, each encoded alone
+    at its own length (rows are independent under the padding mask)."""
+    for b in rows:
+        n = int(lens[b])
+        ref = oracle.encode(ids[b:b + 1, :n])
+        _check(got[b:b + 1, :n], ref, [n])
+        assert np.all(got[b, n:] == 0)
+
+
+def test_xtr_config1_full_batch(xtr_gpu, xtr_oracle):
+    """Config 1 in full: B = 16, L = 128, no padding (M = 2048 takes the
+    2-SM GEMM path on the resident f16 weights)."""
+    ids = np.random.default_rng(1).integers(3, 32128, (16, 128)).astype(np.uint32)
+    raw = xtr_gpu.forward(ids)
+    _check(raw, xtr_oracle.encode(ids), [128] * 16)
+
+
+def test_xtr_config3_lengths_through_encoder(xtr_gpu, xtr_oracle):
+    """Config-3 lengths through the whole encoder: one padded batch of
+    sequences of 512, 257 and 32 tokens (persistent tcgen05 attention with
+    the key padding mask, M = 1536)."""
+    lens = np.array([512, 257, 32], np.int32)
+    ids = np.random.default_rng(31).integers(3, 32128, (3, 512)).astype(np.uint32)
+    out = xtr_gpu.forward(ids, lens)
+    _check_rows(out, ids, lens, range(3), xtr_oracle)
+
+
+def test_xtr_config4_batches_two_lanes(xtr_gpu, xtr_oracle):
+    """Real config-4 batches (about 16k padded tokens each) through the
+    pipelined two-lane entry point wc_t5_forward_many, a seeded sample of 8
+    rows per batch against the oracle.  Three batches put the first and third
+    on one compute lane and the second on the other."""
+    from witchcraft_b200 import shard
+    lengths = shard.config4_lengths()
+    batches = shard.plan_batches(lengths)
+    Ls = np.array([b.L for b in batches])
+    pick = [int(np.argmin(np.abs(Ls - 512))), int(np.argmin(np.abs(Ls - 128))), int(np.argmin(np.abs(Ls - 256)))]
+    rng = np.random.default_rng(41)
+    inputs = []
+    for i in pick:
+        b = batches[i]
+        lens = lengths[b.docs].astype(np.int32)
+        ids = np.zeros((len(b.docs), b.L), np.uint32)
+        for r, n in enumerate(lens):
+            ids[r, :n] = rng.integers(3, 32128, n)
+        assert len(b.docs) * b.L > 12000
+        inputs.append((ids, lens))
+    outs = xtr_gpu.forward_many(inputs)
+    for (ids, lens), out in zip(inputs, outs):
+        rows = sorted(set(rng.choice(len(lens), 7, replace=False).tolist()) | {int(np.argmax(lens))})
+        _check_rows(out, ids, lens, rows, xtr_oracle)
+
+
+def test_forward_many_device_equals_single_calls(tiny_gpu):
+    """wc_t5_forward_many_device (device-resident batches, two compute lanes
+    joined back into the caller's stream) gives every batch exactly its
+    wc_t5_forward_device result."""
+    import torch
+    rng = np.random.default_rng(23)
+    shapes = [(40, 128), (9, 600), (33, 160), (3, 25), (70, 64)]
+    dev, outs, refs = [], [], []
+    for B, L in shapes:
+        ids = torch.from_numpy(rng.integers(3, 512, (B, L)).astype(np.uint32)).cuda()
+        lens = torch.from_numpy(rng.integers(1, L + 1, B).astype(np.int32)).cuda()
+        o = torch.full((B * L, 128), float("nan"), device="cuda")
+        nr = torch.full((B * L,), float("nan"), device="cuda")
+        dev.append((ids, lens))
+        outs.append((o, nr))
+        refs.append((torch.empty_like(o), torch.empty_like(nr)))
+    st = torch.cuda.Stream()
+    tiny_gpu.forward_many_device([(i.data_ptr(), l.data_ptr(), i.shape[0], i.shape[1], o.data_ptr(), n.data_ptr())
+                                  for (i, l), (o, n) in zip(dev, outs)], st.cuda_stream)
+    tiny_gpu.sync(st.cuda_stream)
+    for (i, l), (o, n) in zip(dev, refs):
+        tiny_gpu.forward_device(i.data_ptr(), l.data_ptr(), i.shape[0], i.shape[1], o.data_ptr(), n.data_ptr(), None,
+                                st.cuda_stream)
+    tiny_gpu.sync(st.cuda_stream)
+    for (o, n), (ro, rn) in zip(outs, refs):
+        assert torch.equal(o, ro) and torch.equal(n, rn)

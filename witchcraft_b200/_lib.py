@@ -35,6 +35,8 @@ _SIGNATURES = {
                                              c_void_p, c_void_p]),
     "wc_t5_sync": (c_int, [c_void_p, c_void_p]),
     "wc_t5_forward_many": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "wc_t5_forward_many_device": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p]),
     "wc_t5_dims": (c_int, [c_void_p, _P(c_int), _P(c_int), _P(c_int), _P(c_int)]),
     "wc_q4k_dequant": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     "wc_q4k_dequant_f16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),

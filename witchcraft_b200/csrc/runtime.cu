@@ -64,6 +64,27 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The calling thread's current CUDA context (the device's primary context
+// once the runtime has initialised it), or nullptr.  Per-device caches of
+// device addresses key on it: after a cudaDeviceReset the primary context is
+// a new one and addresses cached under the old one are stale.
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
 // f16 activation matrix [rows][K], box 64 x box_rows, 128-byte swizzle.
 bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t K, uint32_t box_rows = 128) {
   EncodeTiledFn enc = get_encode_fn();
@@ -739,16 +760,23 @@ extern "C" int wc_t5_forward(wc_t5* h, const uint32_t* ids, const int32_t* lengt
 
 namespace {
 uint32_t* kernel_status_word() {
-  // One status word per device for the kernel-level entry points.
+  // One status word per device for the kernel-level entry points, allocated
+  // again when the device's context is not the one it was allocated in (the
+  // device was reset in between).
   static uint32_t* words[64] = {};
+  static CUcontext ctxs[64] = {};
   static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return nullptr;
+  cudaFree(nullptr);  // make the device's primary context current
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lk(mu);
-  if (!words[dev]) {
+  if (!words[dev] || ctxs[dev] != ctx) {
+    words[dev] = nullptr;
     if (cudaMalloc(&words[dev], 4) != cudaSuccess) return nullptr;
     cudaMemset(words[dev], 0, 4);
+    ctxs[dev] = ctx;
   }
   return words[dev];
 }
@@ -950,6 +978,55 @@ extern "C" int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, c
   return check_status(h, cs);
 }
 
+extern "C" int wc_t5_forward_many_device(wc_t5* h, int n, const uint32_t* const* d_ids,
+                                         const int32_t* const* d_lengths, const int* B, const int* L,
+                                         float* const* d_out, float* const* d_norms, void* stream) {
+  if (!h) return WC_E_INVALID_ARG;
+  if (n < 0 || (n > 0 && (!d_ids || !d_lengths || !B || !L || !d_out)))
+    return fail(h, WC_E_INVALID_ARG, "invalid batch arrays");
+  if (n == 0) return WC_OK;
+  int64_t max_rows = 0;
+  int max_b = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!d_ids[i] || !d_lengths[i] || !d_out[i] || B[i] < 1 || L[i] < 1 || L[i] > kMaxL ||
+        static_cast<int64_t>(B[i]) * L[i] > (1 << 26))
+      return fail(h, WC_E_INVALID_ARG, "batch " + std::to_string(i) +
+                                           ": invalid ids/lengths/out pointer or B, L out of range (1 <= L <= 2048)");
+    max_rows = std::max<int64_t>(max_rows, static_cast<int64_t>(B[i]) * L[i]);
+    max_b = std::max(max_b, B[i]);
+  }
+  DeviceGuard g(h->device);
+  static const bool one_lane = [] {
+    const char* v = getenv("WC_FORWARD_LANES");
+    return v && v[0] == '1' && v[1] == 0;
+  }();
+  const bool two_lanes = !one_lane && n > 1 && max_rows > kGraphMaxRows;
+  int rc = ensure_workspace(h, max_rows, max_b);
+  if (!rc && two_lanes) rc = ensure_lane(h, max_rows);
+  if (rc) return rc;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(h->d_status, 0, 4, cs);
+  // the second lane starts after the caller's earlier work and the status reset
+  if (two_lanes && e == cudaSuccess && (e = cudaEventRecord(h->ev_lane, cs)) == cudaSuccess)
+    e = cudaStreamWaitEvent(h->lane_stream, h->ev_lane, 0);
+  if (e != cudaSuccess) return cuda_fail(h, e, "lane fork");
+  for (int i = 0; i < n && rc == WC_OK; ++i) {
+    float* nrm = d_norms ? d_norms[i] : nullptr;
+    if (!two_lanes || (i & 1) == 0)
+      rc = forward_cached(h, d_ids[i], d_lengths[i], B[i], L[i], d_out[i], nrm, nullptr, cs);
+    else
+      rc = forward_on(h, h->lane_x, h->lane_xn, h->lane_qkv, h->lane_att, h->lane_h, h->lane_tm_xn,
+                      h->lane_tm_att, h->lane_tm_h, d_ids[i], d_lengths[i], B[i], L[i], d_out[i], nrm, nullptr,
+                      h->lane_stream);
+  }
+  // join: the caller's stream continues after both lanes (also on an error,
+  // so no work of this call is left unordered behind the caller's stream)
+  if (two_lanes && (e = cudaEventRecord(h->ev_lane, h->lane_stream)) == cudaSuccess)
+    e = cudaStreamWaitEvent(cs, h->ev_lane, 0);
+  if (rc) return rc;
+  return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "lane join");
+}
+
 extern "C" int wc_q4k_dequant_f16(const void* d_blocks, int64_t nblocks, void* d_out_f16, void* stream) {
   if (nblocks < 0 || (nblocks > 0 && (!d_blocks || !d_out_f16))) return WC_E_INVALID_ARG;
   return q4k_dequant_f16_launch(static_cast<const uint8_t*>(d_blocks), nblocks, static_cast<__half*>(d_out_f16),
@@ -1129,22 +1206,27 @@ NoAllocLayout noalloc_layout(const wc_t5* h, int64_t M) {
 }
 
 // Device address of g_noalloc_scratch on the current device.  Looked up once
-// per device (the host-side name of a __device__ array is not a device
-// address); this first lookup also loads the module on that device.
+// per device and context (the host-side name of a __device__ array is not a
+// device address); this first lookup also loads the module on that device.
+// If the device was reset since, its context is a new one and the address is
+// looked up again rather than reused.
 uint8_t* noalloc_scratch_ptr(int dev, cudaError_t* err) {
   static uint8_t* ptrs[64] = {};
+  static CUcontext ctxs[64] = {};
   static std::mutex mu;
   *err = cudaSuccess;
   if (dev < 0 || dev >= 64) {
     *err = cudaErrorInvalidDevice;
     return nullptr;
   }
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lk(mu);
-  if (!ptrs[dev]) {
+  if (!ptrs[dev] || ctxs[dev] != ctx) {
     void* p = nullptr;
     *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (*err != cudaSuccess) return nullptr;
     ptrs[dev] = static_cast<uint8_t*>(p);
+    ctxs[dev] = ctx;
   }
   return ptrs[dev];
 }
@@ -1278,6 +1360,7 @@ extern "C" int wc_selftest_wait_timeout(uint64_t limit_ns) {
 // Milliseconds between consecutive marks of the last forward; returns the count.
 extern "C" int wc_fwd_events(float* ms, int max) {
   const int n = wc::g_fwd_n;
+  if (n < 2) return 0;
   cudaEventSynchronize(wc::g_fwd_ev[n - 1]);
   for (int i = 1; i < n && i <= max; ++i) cudaEventElapsedTime(&ms[i - 1], wc::g_fwd_ev[i - 1], wc::g_fwd_ev[i]);
   return n - 1;

@@ -110,6 +110,18 @@ class T5EncoderModel:
                                          ctypes.c_void_p(d_outn) if d_outn else None,
                                          ctypes.c_void_p(stream) if stream else None), self._h)
 
+    def forward_many_device(self, batches, stream: int | None = None) -> None:
+        """Enqueue device-resident batches [(d_ids, d_lengths, B, L, d_out, d_norms or None)]
+        (raw device pointers) in one call on `stream` (wc_t5_forward_many_device)."""
+        n = len(batches)
+        vp = ctypes.c_void_p
+        col = lambda k: (vp * n)(*[vp(b[k]) if b[k] else None for b in batches])  # noqa: E731
+        Bs = (ctypes.c_int * n)(*[b[2] for b in batches])
+        Ls = (ctypes.c_int * n)(*[b[3] for b in batches])
+        norms = col(5) if any(b[5] for b in batches) else None
+        check(lib().wc_t5_forward_many_device(self._h, n, col(0), col(1), Bs, Ls, col(4), norms,
+                                              vp(stream) if stream else None), self._h)
+
     def sync(self, stream: int | None = None) -> None:
         check(lib().wc_t5_sync(self._h, ctypes.c_void_p(stream) if stream else None), self._h)
 
