@@ -10,12 +10,18 @@ count on every rank: weak scaling), through the full 12-layer XTR-base
 encoder (random-init N(0, 0.02) weights quantized to Q4_K; synthetic ids).
 The metric is valid (unpadded) encoder tokens per second over all ranks.
 
-  value  device-resident inputs, kernel time of the K steps (CUDA events on
-         the launching stream, barrier + synchronize on both sides, max over
-         ranks)
-  e2e    the public C ABI call wc_t5_forward with pinned host buffers: the
-         H2D copy of ids/lengths and the D2H copy of the raw [B,L,128]
-         projection and norms are inside the timed region
+  value  device-resident inputs, one wc_t5_forward_many_device call per step
+         (the handle's two compute lanes), device time of the K steps (CUDA
+         events on the launching stream, barrier + synchronize on both sides,
+         max over ranks)
+  e2e    the public C ABI call wc_t5_forward_many with page-locked host
+         buffers, one call per step: the H2D copy of ids/lengths and the D2H
+         copy of the raw [B,L,128] projection and norms are inside the timed
+         region
+  corpus the whole corpus once, dealt to the ranks by LPT and encoded through
+         witchcraft_b200.pool (strong scaling, wall clock, max over ranks)
+Clocks are sampled by one nvidia-smi process (on local rank 0) for all GPUs
+of the job during each timed region.
 Multi-GPU: one process per GPU (torchrun), each rank a replica with its own
 batches; no collective on the data path (NCCL only for the barrier and the
 max-over-ranks of the timings).
@@ -40,9 +46,10 @@ METRIC = "encoder tokens/sec XTR-base Q4_K (bulk embedding, config 4)"
 UNIT = "tokens/s"
 MAX_BATCH_TOKENS = 16384
 LAUNCHES_PER_FORWARD_PER_LAYER = 7   # qkv gemm, attention, o gemm, rmsnorm, wi gemm, wo gemm, rmsnorm
-# dram read+write bytes per launch of the dominant kernel from the committed ncu
-# capture at M = 16,384.
-NCU_TRAFFIC_BYTES = 49226240  # 31.49 MB read + 17.74 MB written, profiles/gemm2_geglu_f16_m16384.md
+# dram read+write bytes per launch of the dominant kernel (the gated-GELU GEMM
+# at M = 16,384), from one ncu capture of `bench.py --profile-kernel geglu`
+# (dram__bytes_read.sum + dram__bytes_write.sum); re-captured when the kernel changes
+NCU_TRAFFIC_BYTES = 49226240  # 31.49 MB read + 17.74 MB written
 
 
 def _peaks():
@@ -54,10 +61,11 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled during the timed region: one
+    sampler process (on local rank 0) covering every GPU of the job."""
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, indices):
+        self.index = ",".join(str(i) for i in indices)
         self.rows = []
         self._stop = threading.Event()
         self._t = None
@@ -191,6 +199,15 @@ def run_reference(args):
     }), flush=True)
 
 
+def _gpu_indices(world: int):
+    """Physical indices of the job's GPUs (local ranks 0..world-1) for nvidia-smi."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        return ids[:world]
+    return list(range(world))
+
+
 def run_ours(args):
     import torch
     world, rank, local = _dist_env()
@@ -220,6 +237,10 @@ def run_ours(args):
         torch.distributed.all_reduce(t)
         return float(t.item())
 
+    def sampler():
+        # one nvidia-smi process for the whole job (local rank 0), not one per rank
+        return ClockSampler(_gpu_indices(world)).start() if local == 0 else None
+
     model = make_synthetic_model(seed=0)
     enc = T5EncoderModel(model.gguf, model.config.to_json(), device=local)
     n_layers = model.config.num_layers
@@ -227,49 +248,41 @@ def run_ours(args):
     lengths, mine = _plan(world, rank, per_step, args.warmup + args.steps)
     rng = np.random.default_rng(1000 + rank)
     host_inputs = [_make_inputs(lengths, b, rng) for b in mine]
-    # Device-resident leg: two handles of the same weights on two streams take
-    # alternate batches, as wc_t5_forward_many's two compute lanes do, so one
-    # batch's memory-bound kernels share the SMs with the other's GEMMs.
-    stream, stream2 = torch.cuda.Stream(), torch.cuda.Stream()
-    lanes = [(enc, stream)]
-    if args.lanes == 2:
-        lanes.append((T5EncoderModel(model.gguf, model.config.to_json(), device=local), stream2))
-    dev = []
+    # Device-resident leg: one wc_t5_forward_many_device call per step, which
+    # puts alternate batches on the handle's two compute lanes (one batch's
+    # memory-bound kernels share the SMs with the other's GEMMs).
+    stream = torch.cuda.Stream()
     max_rows = max(b.padded_tokens for b in mine)
-    d_outs = [(torch.empty(max_rows, 128, device="cuda"), torch.empty(max_rows, device="cuda")) for _ in lanes]
-    for ids, lens in host_inputs:
-        dev.append((torch.from_numpy(ids).cuda(), torch.from_numpy(lens).cuda()))
+    d_outs = [(torch.empty(max_rows, 128, device="cuda"), torch.empty(max_rows, device="cuda"))
+              for _ in range(per_step)]
+    dev = [(torch.from_numpy(ids).cuda(), torch.from_numpy(lens).cuda()) for ids, lens in host_inputs]
     torch.cuda.synchronize()
 
     def step(s: int):
+        batch = []
         for j in range(per_step):
-            i = s * per_step + j
-            ids, lens = dev[i]
-            B, L = ids.shape
-            e, st = lanes[j % len(lanes)]
-            o, nr = d_outs[j % len(lanes)]
-            e.forward_device(ids.data_ptr(), lens.data_ptr(), B, L, o.data_ptr(), nr.data_ptr(), None,
-                             st.cuda_stream)
+            ids, lens = dev[s * per_step + j]
+            o, nr = d_outs[j]
+            batch.append((ids.data_ptr(), lens.data_ptr(), ids.shape[0], ids.shape[1], o.data_ptr(), nr.data_ptr()))
+        enc.forward_many_device(batch, stream.cuda_stream)
 
     # ---- device-resident timed region
     for s in range(args.warmup):
         step(s)
+    enc.sync(stream.cuda_stream)
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local).start()
+    clocks = sampler()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    stream2.wait_event(e0)
     for s in range(args.warmup, args.warmup + args.steps):
         step(s)
-    stream.wait_stream(stream2)
     e1.record(stream)
-    for e, st in lanes:
-        e.sync(st.cuda_stream)
+    enc.sync(stream.cuda_stream)
     torch.cuda.synchronize()
-    clk = clocks.stop()
     barrier()
+    clk = clocks.stop() if clocks else None
     ms = e0.elapsed_time(e1)
     ms_max = max_over_ranks(ms)
     timed = range(args.warmup * per_step, (args.warmup + args.steps) * per_step)
@@ -304,14 +317,26 @@ def run_ours(args):
     for s0 in range(0, len(warm), per_step):
         e2e_step(warm[s0:s0 + per_step])
     barrier()
+    clocks = sampler()
     t0 = time.perf_counter()
     for s0 in range(0, len(timed), per_step):
         e2e_step(timed[s0:s0 + per_step])
-    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    t_local = time.perf_counter() - t0
     barrier()
+    clk_e2e = clocks.stop() if clocks else None
+    t_e2e = max_over_ranks(t_local)
     h2d = sum(pinned[i][0].numel() * 4 + pinned[i][1].numel() * 4 for i in timed) / args.steps
     d2h = sum(pinned[i][2].numel() * 4 + pinned[i][3].numel() * 4 for i in timed) / args.steps
     e2e_value = all_valid / t_e2e
+    del pinned
+
+    fused = None
+    if rank == 0 and not args.no_extras:
+        fused = fused_weights_leg(model, dev, host_inputs, d_outs, per_step, args, lengths)
+
+    corpus = None
+    if args.corpus:
+        corpus = corpus_measurement(model, enc, world, rank, local, barrier, max_over_ranks)
 
     result = None
     if rank == 0:
@@ -319,7 +344,8 @@ def run_ours(args):
         roof = None
         extras = {}
         if not args.no_extras:
-            roof, extras = kernel_measurements(enc, args, peak, peak_src)
+            roof, extras = kernel_measurements(enc, args, peak, peak_src, cpu=world == 1 and not args.no_cpu,
+                                               model=model)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -331,12 +357,18 @@ def run_ours(args):
                        "padded_tokens_per_rank_step": padded_tokens / args.steps,
                        "valid_tokens_per_rank_step": valid_tokens / args.steps,
                        "parallelism": f"replicas x{world} (no data-path collective)",
+                       "value_api": "wc_t5_forward_many_device, one call per step (two compute lanes)",
                        "l2": "per-batch working set (activations of up to 16,384 tokens, ~250 MB) exceeds the 126 MB L2"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                    "api": "wc_t5_forward_many (page-locked host buffers, one call per step, copies overlap the forwards)"},
+                    "api": "wc_t5_forward_many (page-locked host buffers, one call per step, copies overlap the forwards)",
+                    "clocks": clk_e2e},
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if corpus:
+            result["corpus"] = corpus
+        if fused:
+            result["bulk_fused_q4k"] = fused
         if roof:
             result["roofline"] = roof
         result.update(extras)
@@ -346,6 +378,91 @@ def run_ours(args):
     enc.close()
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def fused_weights_leg(model, dev, host_inputs, d_outs, per_step, args, lengths):
+    """The device-resident bulk leg on a handle created with WC_F16_WEIGHTS=0:
+    the large-M GEMMs dequantise the Q4_K super-blocks in the kernel (TMA-
+    staged raw blocks, dequant warps, tcgen05) instead of reading the resident
+    f16 copies.  Same batches, same timing method, this rank's GPU only."""
+    import torch
+    from witchcraft_b200.t5cuda import T5EncoderModel
+    os.environ["WC_F16_WEIGHTS"] = "0"
+    try:
+        enc = T5EncoderModel(model.gguf, model.config.to_json(), device=torch.cuda.current_device())
+    finally:
+        del os.environ["WC_F16_WEIGHTS"]
+    stream = torch.cuda.Stream()
+
+    def step(s):
+        batch = []
+        for j in range(per_step):
+            ids, lens = dev[s * per_step + j]
+            o, nr = d_outs[j]
+            batch.append((ids.data_ptr(), lens.data_ptr(), ids.shape[0], ids.shape[1], o.data_ptr(), nr.data_ptr()))
+        enc.forward_many_device(batch, stream.cuda_stream)
+    for s in range(args.warmup):
+        step(s)
+    enc.sync(stream.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.warmup, args.warmup + args.steps):
+        step(s)
+    e1.record(stream)
+    enc.sync(stream.cuda_stream)
+    ms = e0.elapsed_time(e1)
+    enc.close()
+    timed = range(args.warmup * per_step, (args.warmup + args.steps) * per_step)
+    valid = float(sum(int(host_inputs[i][1].sum()) for i in timed))
+    return {"what": "device-resident bulk leg, Q4_K dequantised inside the large-M GEMMs (WC_F16_WEIGHTS=0)",
+            "tokens_per_s": valid / (ms / 1e3), "ms_per_step": ms / args.steps}
+
+
+def corpus_measurement(model, enc, world, rank, local, barrier, max_over_ranks):
+    """The whole config-4 corpus (131,072 documents, about 23.8 M valid tokens)
+    encoded once across the job's GPUs: batches dealt to ranks by LPT on
+    padded tokens (shard.assign_batches), each rank running its share through
+    the product's bulk pool (witchcraft_b200.pool: page-locked output ring,
+    wc_t5_forward_many per chunk, results handed to a sink in host memory).
+    Wall-clock from a barrier to the last rank's last result (max over ranks):
+    strong scaling, the total work is fixed."""
+    from witchcraft_b200 import shard
+    from witchcraft_b200.pool import EncoderPool
+    lengths = shard.config4_lengths()
+    batches = shard.plan_batches(lengths, MAX_BATCH_TOKENS)
+    owners = shard.assign_batches(batches, world)[rank]
+    rng = np.random.default_rng(77 + rank)
+    mine = []
+    for i in owners:
+        b = batches[i]
+        lens = lengths[b.docs].astype(np.int32)
+        ids = rng.integers(3, 32128, (len(lens), b.L)).astype(np.uint32)
+        ids[np.arange(b.L)[None, :] >= lens[:, None]] = 0
+        mine.append((ids, lens))
+    valid = float(sum(int(l.sum()) for _, l in mine))
+    done = [0]
+
+    def sink(i, raw, norms):
+        done[0] += 1
+    with EncoderPool(lambda d: enc, [local], chunk=8, max_batch_tokens=MAX_BATCH_TOKENS,
+                     close_encoders=False) as pool:
+        pool.run(mine[:8], sink)  # warm-up of the ring and the lanes
+        barrier()
+        t0 = time.perf_counter()
+        pool.run(mine, sink)
+        t = time.perf_counter() - t0
+    barrier()
+    t_max = max_over_ranks(t)
+    total_valid = valid
+    if world > 1:
+        import torch
+        v = torch.tensor([valid], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(v)
+        total_valid = float(v.item())
+    return {"what": "whole config-4 corpus (131,072 docs) once across all ranks, LPT-dealt batches, "
+                    "witchcraft_b200.pool + wc_t5_forward_many, page-locked outputs in host memory",
+            "scaling": "strong", "docs": int(len(lengths)), "batches": len(batches),
+            "valid_tokens": total_valid, "wall_s": t_max, "tokens_per_s": total_valid / t_max}
 
 
 def _time_launches(fn, stream, reps: int, warm: int = 3) -> float:
@@ -368,7 +485,7 @@ def _time_launches(fn, stream, reps: int, warm: int = 3) -> float:
     return a.elapsed_time(b) / reps / 1e3  # seconds per launch
 
 
-def kernel_measurements(enc, args, peak, peak_src):
+def kernel_measurements(enc, args, peak, peak_src, cpu=False, model=None):
     """Per-kernel timings for the roofline: the gated-GELU GEMM (the dominant
     kernel, 44% of encoder FLOPs) at one full batch (M = 16,384) on the
     resident f16 weights the forward uses from 512 rows, plus the other GEMM
@@ -429,8 +546,104 @@ def kernel_measurements(enc, args, peak, peak_src):
     t = _time_launches(f, st, reps=20)
     afl = float(sum(12 * 4 * 64 * int(n) ** 2 for n in lens))
     micro["attention_config3"] = {"us": t * 1e6, "tflops": afl / t / 1e12, "frac_of_peak": afl / t / 1e12 / peak}
-    return roof, {"microbench": micro, "query_latency": query_latency(enc), "codec": codec_measurement(),
-                  "index_assign": assign_measurement(), "query_scoring": query_scoring_measurement()}
+    c1 = config1_measurement(enc, peak)
+    extras = {"microbench": micro, "config1": c1, "query_latency": query_latency(enc), "codec": codec_measurement(),
+              "index_assign": assign_measurement(), "query_scoring": query_scoring_measurement()}
+    if cpu and model is not None:
+        extras["cpu_configs"] = cpu_config_baselines(model, lens)
+    return roof, extras
+
+
+CONFIG1_FLOP_PER_TOKEN = 2.0 * (12 * 7077888 + 98304) + 12 * 3072 * 128  # 174.78 MFLOP
+
+
+def config1_measurement(enc, peak, reps: int = 50):
+    """Config 1: the full encoder on one B = 16 x L = 128 batch (no padding),
+    device-resident, CUDA events around `reps` forwards on one stream."""
+    import torch
+    rng = np.random.default_rng(1)
+    ids = torch.from_numpy(rng.integers(3, 32128, (16, 128)).astype(np.uint32)).cuda()
+    lens = torch.full((16,), 128, dtype=torch.int32, device="cuda")
+    out = torch.empty(16 * 128, 128, device="cuda")
+    st = torch.cuda.Stream()
+    f = lambda: enc.forward_device(ids.data_ptr(), lens.data_ptr(), 16, 128, out.data_ptr(), None, None,  # noqa
+                                   st.cuda_stream)
+    t = _time_launches(f, st, reps=reps)
+    enc.sync(st.cuda_stream)
+    tok = 16 * 128 / t
+    return {"what": "full encoder, B=16 x L=128, device-resident", "tokens_per_s": tok, "ms_per_batch": t * 1e3,
+            "tflops": tok * CONFIG1_FLOP_PER_TOKEN / 1e12, "frac_of_peak": tok * CONFIG1_FLOP_PER_TOKEN / 1e12 / peak}
+
+
+def cpu_config_baselines(model, attn_lens, budget_s: float = 8.0):
+    """The reference's f32 CPU algorithm (oracle/torch_ref.py, torch MKL on
+    every host core) beside configs 1, 2, 3 and 5: the config-1 batch encoded
+    one sequence at a time, the config-2 GEMMs in f32 (gated GELU included),
+    config-3 attention per sequence at its valid length (softmax(QK^T + bias) V
+    without scaling), and 32-token query latency p50/p99 at batch 1 and 256
+    (queries encoded one by one, as the reference's Embedder does)."""
+    import torch
+    from oracle.torch_ref import TorchCPUEncoder
+    cores = os.cpu_count() or 1
+    enc = TorchCPUEncoder(model, threads=cores)
+    res = {"cores": cores, "kind": "port", "impl": "oracle/torch_ref.py (torch CPU f32, MKL GEMMs)"}
+    rng = np.random.default_rng(1)
+    ids = rng.integers(3, 32128, (16, 128))
+    enc.encode_one(ids[0])
+    t0 = time.perf_counter()
+    for r in ids:
+        enc.encode_one(r)
+    res["config1_tokens_per_s"] = 16 * 128 / (time.perf_counter() - t0)
+    g = {}
+    with torch.no_grad():
+        for name, (M, K, N, gated) in {"qkv_M8192": (8192, 768, 2304, False), "wi_geglu_M8192": (8192, 768, 2048, True),
+                                       "wo_M8192": (8192, 2048, 768, False), "o_M8192": (8192, 768, 768, False)}.items():
+            x = torch.randn(M, K)
+            w0 = torch.randn(N, K) * 0.02
+            w1 = torch.randn(N, K) * 0.02
+
+            def f():
+                a = x @ w0.T
+                if gated:
+                    a = 0.5 * a * (1 + torch.tanh(0.7978845608 * (a + 0.044715 * a ** 3))) * (x @ w1.T)
+                return a
+            f()
+            t0 = time.perf_counter()
+            n = 0
+            while n < 3 or (time.perf_counter() - t0 < 0.5 and n < 20):
+                f()
+                n += 1
+            t = (time.perf_counter() - t0) / n
+            g[name] = {"ms": t * 1e3, "tflops": 2.0 * M * K * N * (2 if gated else 1) / t / 1e12}
+        res["config2_gemm"] = g
+        H = 12
+        afl = float(sum(12 * 4 * 64 * int(n) ** 2 for n in attn_lens))
+        t0 = time.perf_counter()
+        for L in attn_lens:
+            L = int(L)
+            q, k, v = (torch.randn(H, L, 64) for _ in range(3))
+            bias = enc._bias(L)
+            torch.softmax(q @ k.transpose(-1, -2) + bias, -1) @ v
+        t = time.perf_counter() - t0
+        res["config3_attention"] = {"ms": t * 1e3, "tflops": afl / t / 1e12}
+    qrng = np.random.default_rng(6)
+    q = {}
+    for B, runs in ((1, 100), (256, 3)):
+        times = []
+        t_start = time.perf_counter()
+        for r in range(runs):
+            lens = qrng.integers(4, 33, B)
+            toks = [qrng.integers(3, 32128, int(n)) for n in lens]
+            t0 = time.perf_counter()
+            for tk in toks:
+                enc.encode_one(tk)
+            times.append((time.perf_counter() - t0) * 1e3)
+            if time.perf_counter() - t_start > budget_s:
+                break
+        q[f"b{B}"] = {"p50_ms": float(np.percentile(times, 50)), "p99_ms": float(np.percentile(times, 99)),
+                      "runs": len(times)}
+    res["config5_query_latency"] = q
+    return res
 
 
 def query_scoring_measurement(rows: int = 200000, m: int = 32, per_sub: int = 8):
@@ -462,11 +675,32 @@ def query_scoring_measurement(rows: int = 200000, m: int = 32, per_sub: int = 8)
     for _ in range(5):
         Qm.score_gpu(c, table)
     tg = (time.perf_counter() - t0) / 5
+    # the scoring kernel alone on device-resident inputs (CUDA events)
+    from witchcraft_b200._lib import lib
+    dev = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a, dt)).cuda()  # noqa: E731
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    dq, dcodes, dcl = dev(q, np.float32), dev(codes.reshape(-1), np.uint8), dev(cluster.view(np.int32), np.int32)
+    dcs, dtab = dev(cs, np.float32), dev(table, np.float32)
+    dgr, dgs, dds = (dev(a, np.int64) for a in (c.group_rows, c.group_start, c.doc_start))
+    dmiss = dev(c.missing, np.float32)
+    out = torch.empty(n_groups, dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    f = lambda: lib().wc_score_candidates(P(dq), m, 128, P(dcodes), P(dcl), P(dcs), n_cent, P(dtab), rows, None,  # noqa
+                                          P(dgr), P(dgs), P(dds), len(c.doc_start) - 1, P(dmiss), P(out),
+                                          ctypes.c_void_p(st.cuda_stream))
+    tk = _time_launches(f, st, reps=20)
+    # bytes the kernel must read once: codes, cluster ids, row/group/doc
+    # offsets, centroid scores, query, plus the scores it writes
+    kbytes = (codes.nbytes + rows * 4 + rows * 8 + (n_groups + 1) * 8 + (len(c.doc_start)) * 8 + cs.nbytes + q.nbytes
+              + n_groups * 4)
+    _, _, hbm, _ = _peaks()
     t0 = time.perf_counter()
     O.score_candidates(q, codes, cluster, cs, table, c.raw, c.group_rows, c.group_start, c.doc_start, c.missing)
     tc = time.perf_counter() - t0
     return {"what": "candidate scoring of one query (m tokens x rows, 4-bit residuals)", "m": m, "rows": rows,
-            "gpu_ms_with_copies": tg * 1e3, "cpu_oracle_ms_1core": tc * 1e3}
+            "gpu_ms_with_copies": tg * 1e3, "gpu_kernel_us": tk * 1e6, "kernel_bytes": kbytes,
+            "kernel_gbs": kbytes / tk / 1e9, "frac_of_hbm": kbytes / tk / 1e9 / hbm,
+            "cpu_oracle_ms_1core": tc * 1e3}
 
 
 def assign_measurement(m: int = 262144, cpu_rows: int = 256):
@@ -627,6 +861,8 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=8.0)
     ap.add_argument("--no-extras", action="store_true", help="skip per-kernel timings and query latency")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-corpus", dest="corpus", action="store_false",
+                    help="skip the whole-corpus (strong scaling) encode")
     ap.add_argument("--lanes", type=int, choices=[1, 2], default=2,
                     help="device-resident leg: encoder handles on their own streams taking alternate batches")
     ap.add_argument("--profile-kernel", choices=["geglu", "qkv", "wo", "attention"], default=None,

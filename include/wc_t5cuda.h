@@ -11,8 +11,10 @@
  * (the OpenVINO backend implements the same surface, src/openvino_t5.rs:151-245).
  *
  * Conventions
- *   - Every function returns 0 (WC_OK) on success or a negative WC_E* code.
- *     Nothing aborts, throws or exits across this boundary.
+ *   - Every function returns 0 (WC_OK) on success or a negative WC_E* code;
+ *     the forward calls may also return the positive warning
+ *     WC_W_F16_CLIPPED (results delivered, see below).  Nothing aborts,
+ *     throws or exits across this boundary.
  *   - The caller owns all host buffers.  A handle owns its device memory,
  *     stream and workspaces; wc_t5_destroy frees them.
  *   - One handle drives one GPU.  A handle is not re-entrant (wrap it in a
@@ -22,7 +24,12 @@
  *   - Numerics: the residual stream, RMSNorm statistics, every accumulation
  *     and all outputs are f32; tensor-core operands (normalised activations,
  *     dequantised weights, Q/K/V, softmax weights, gated-GELU output) are f16
- *     (11-bit significand), saturated to the finite f16 range.
+ *     (11-bit significand), saturated to the finite f16 range.  A forward in
+ *     which any such value was clipped (|x| >= 65520, or NaN) returns
+ *     WC_W_F16_CLIPPED instead of WC_OK: the outputs are written, but they
+ *     may deviate from the reference's f32 computation beyond the stated
+ *     tolerance.  (The f32 reference has no such limit; a checkpoint whose
+ *     activations leave the f16 range needs a wider operand type.)
  *   - Functions taking `void* stream` accept a cudaStream_t (NULL = legacy
  *     default stream) and device pointers; they return once the work is
  *     enqueued.
@@ -38,6 +45,7 @@ extern "C" {
 #endif
 
 enum {
+  WC_W_F16_CLIPPED = 1,    /* success, but an f16 activation was clipped (see Numerics) */
   WC_OK = 0,
   WC_E_INVALID_ARG = -1,   /* null pointer, bad size, token id >= vocab, ... */
   WC_E_GGUF = -2,          /* malformed or truncated GGUF, missing tensor */
@@ -52,11 +60,23 @@ typedef struct wc_t5 wc_t5;
 /* Number of CUDA devices visible to this process (0 when none; never fails). */
 int wc_t5_device_count(void);
 
+/* Page-locked host memory (cudaHostAlloc, portable across devices) for the
+ * ids / outputs of wc_t5_forward_many, whose copies overlap the compute only
+ * from page-locked buffers.  Returns NULL on failure.  No reference
+ * counterpart (the reference keeps results in candle host tensors). */
+void* wc_host_alloc(size_t bytes);
+void wc_host_free(void* p);
+
 /* Build an encoder on device `device_ordinal` from the bytes of xtr.gguf and
  * the text of config.json (T5ModelBuilder::load + build_encoder,
  * src/quantized_t5.rs:713-749).  Q4_K tensors are uploaded unchanged (raw
- * super-blocks); F32/F16 tensors are uploaded as f32.  On failure *out is set
- * to NULL and the reason is available from wc_t5_last_error(NULL). */
+ * super-blocks); F32/F16 tensors are uploaded as f32.  The layer matrices are
+ * also dequantised once to resident f16 copies (170 MB for XTR-base) that the
+ * GEMMs of batches of 512 tokens and more read; with the environment variable
+ * WC_F16_WEIGHTS=0 set at create time the handle keeps only the Q4_K bytes
+ * and those GEMMs dequantise the super-blocks in the kernel instead (same
+ * operand bits, same results).  On failure *out is set to NULL and the reason
+ * is available from wc_t5_last_error(NULL). */
 int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf_len, const char* config_json,
                  wc_t5** out);
 

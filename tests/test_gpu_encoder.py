@@ -282,3 +282,22 @@ def test_forward_many_device_equals_single_calls(tiny_gpu):
     tiny_gpu.sync(st.cuda_stream)
     for (o, n), (ro, rn) in zip(outs, refs):
         assert torch.equal(o, ro) and torch.equal(n, rn)
+
+
+def test_fused_q4k_weights_handle_bitwise(xtr_model, xtr_gpu):
+    """A handle created with WC_F16_WEIGHTS=0 keeps no f16 weight copies; its
+    large-M GEMMs dequantise the Q4_K super-blocks in the kernel into the same
+    f16 operand bits, so every output equals the default handle's."""
+    os.environ["WC_F16_WEIGHTS"] = "0"
+    try:
+        fused = T5EncoderModel(xtr_model.gguf, xtr_model.config.to_json(), 0)
+    finally:
+        del os.environ["WC_F16_WEIGHTS"]
+    try:
+        rng = np.random.default_rng(51)
+        for B, L in ((16, 128), (3, 300), (40, 200)):
+            ids = rng.integers(3, 32128, (B, L)).astype(np.uint32)
+            lens = rng.integers(1, L + 1, B).astype(np.int32)
+            np.testing.assert_array_equal(fused.forward(ids, lens), xtr_gpu.forward(ids, lens))
+    finally:
+        fused.close()

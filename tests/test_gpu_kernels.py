@@ -191,7 +191,11 @@ def _attention_torch(qkv, B, L, H, lengths, bias_tab):
                                          (2, 65, [65, 33]), (1, 2048, [2048]), (3, 1, [1, 1, 1]),
                                          # L <= 64: the mma.sync kernel of short batches
                                          (4, 32, [32, 17, 1, 5]), (2, 64, [64, 40]), (3, 17, [17, 9, 16]),
-                                         (2, 2, [2, 1]), (2, 33, [33, 20]), (3, 31, [0, 31, 7])])
+                                         (2, 2, [2, 1]), (2, 33, [33, 20]), (3, 31, [0, 31, 7]),
+                                         # 65 <= L <= 1024: the two-tile kernel (pairs of query tiles of
+                                         # one head, or the last tile of two heads when the count is odd)
+                                         (3, 300, [0, 300, 129]), (2, 384, [300, 384]), (1, 1024, [1024]),
+                                         (5, 129, [129, 128, 127, 64, 65]), (2, 1025, [1025, 700])])
 def test_attention_matches_oracle(B, L, lengths):
     H = 12
     g = torch.Generator().manual_seed(B * 1000 + L)
@@ -206,6 +210,22 @@ def test_attention_matches_oracle(B, L, lengths):
         rows = slice(b * L, b * L + lengths[b])
         err = np.abs(out[rows] - ref[rows]).max()
         assert err < 2e-2, (b, err)
+
+
+@pytest.mark.parametrize("H", [2, 6, 3, 16])
+def test_attention_head_counts(H):
+    """Even head counts up to 16 take the two-tile kernel; an odd count the
+    single-tile one.  Both against the fp32 torch reference."""
+    B, L = 3, 260
+    lengths = [260, 131, 77]
+    qkv = torch.randn(B * L, 3 * H * 64, generator=torch.Generator().manual_seed(H)).to(torch.float16).cuda()
+    bias_tab = (np.random.default_rng(H).standard_normal((32, H)) * 0.1).astype(np.float32)
+    out = _attention_gpu(qkv, B, L, H, lengths, bias_tab).float()
+    ref = _attention_torch(qkv, B, L, H, lengths, bias_tab)
+    for b in range(B):
+        rows = slice(b * L, b * L + lengths[b])
+        assert (out[rows] - ref[rows]).abs().max().item() < 2e-2, b
+        assert not out[b * L + (lengths[b] + 127) // 128 * 128:(b + 1) * L].any()
 
 
 def test_attention_config3_against_torch():

@@ -15,6 +15,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 HEADER = os.path.join(INCLUDE, "wc_t5cuda.h")
 
 WC_OK = 0
+WC_W_F16_CLIPPED = 1
 ERRORS = {-1: "WC_E_INVALID_ARG", -2: "WC_E_GGUF", -3: "WC_E_UNSUPPORTED", -4: "WC_E_CUDA",
           -5: "WC_E_TIMEOUT", -6: "WC_E_CONFIG"}
 
@@ -37,6 +38,8 @@ _SIGNATURES = {
     "wc_t5_forward_many": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "wc_t5_forward_many_device": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_void_p]),
+    "wc_host_alloc": (c_void_p, [c_size_t]),
+    "wc_host_free": (None, [c_void_p]),
     "wc_t5_dims": (c_int, [c_void_p, _P(c_int), _P(c_int), _P(c_int), _P(c_int)]),
     "wc_q4k_dequant": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
     "wc_q4k_dequant_f16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
@@ -94,7 +97,17 @@ def header_symbols() -> list[str]:
     return sorted(names)
 
 
+class F16ClipWarning(RuntimeWarning):
+    """A forward clipped an f16 activation to +-65504 (WC_W_F16_CLIPPED): its
+    outputs were written but may deviate from the f32 reference."""
+
+
 def check(code: int, handle=None) -> None:
+    if code == WC_W_F16_CLIPPED:
+        import warnings
+        msg = lib().wc_t5_last_error(handle)
+        warnings.warn(msg.decode() if msg else "f16 activation clipped", F16ClipWarning, stacklevel=3)
+        return
     if code != WC_OK:
         msg = lib().wc_t5_last_error(handle)
         raise WcError(code, msg.decode() if msg else "")

@@ -76,6 +76,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 enum : uint32_t {
   kStatusWaitTimeout = 1u,   // an mbarrier wait ran past its time limit
   kStatusBadArgument = 2u,   // a kernel saw a shape it does not support
+  kStatusF16Clipped = 4u,    // an f16 activation store clipped a value (|x| >= 65520 or NaN) to +-65504
 };
 
 // Wall-clock limit for any single spin-wait inside a kernel (ns).  A healthy
@@ -284,6 +285,23 @@ __device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// A value the f16 conversion cannot represent: round-to-nearest would give
+// inf (|x| >= 65520) or it is NaN.  The saturating stores clip it to +-65504.
+__device__ __forceinline__ bool f16_clips(float x) { return !(fabsf(x) < 65520.f); }
+
+// pack_f16x2_sat that also records in `clip` whether either value was clipped.
+__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi, bool& clip) {
+  clip |= f16_clips(lo) | f16_clips(hi);
+  return pack_f16x2_sat(lo, hi);
+}
+
+// Sets kStatusF16Clipped in *status when this thread clipped a value.  The
+// flag is read first so a kernel that clips everywhere issues few atomics.
+__device__ __forceinline__ void report_f16_clip(bool clip, uint32_t* status) {
+  if (clip && status && !(*reinterpret_cast<volatile uint32_t*>(status) & kStatusF16Clipped))
+    atomicOr(status, kStatusF16Clipped);
 }
 
 // Packed f32x2 arithmetic (one instruction for two lanes of f32 on sm_100).

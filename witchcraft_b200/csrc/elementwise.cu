@@ -54,7 +54,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const uint32_t* __restrict__ ids,
                                      const int32_t* __restrict__ lengths, int L, int M, int D,
                                      const float* __restrict__ w, float eps, float* __restrict__ x,
-                                     __half* __restrict__ xn) {
+                                     __half* __restrict__ xn, uint32_t* __restrict__ status) {
   pdl_wait();
   pdl_launch_next();  // after the wait: at most one grid waits ahead
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -78,6 +78,7 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
   }
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+  bool clip = false;
 #pragma unroll
   for (int c = 0; c < kMaxD / 256; ++c) {
     if (c < nb) {
@@ -88,27 +89,29 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
       const float4 w0 = reinterpret_cast<const float4*>(w + e)[0];
       const float4 w1 = reinterpret_cast<const float4*>(w + e)[1];
       uint4 o;
-      o.x = pack_f16x2_sat(v[c][0] * inv * w0.x, v[c][1] * inv * w0.y);
-      o.y = pack_f16x2_sat(v[c][2] * inv * w0.z, v[c][3] * inv * w0.w);
-      o.z = pack_f16x2_sat(v[c][4] * inv * w1.x, v[c][5] * inv * w1.y);
-      o.w = pack_f16x2_sat(v[c][6] * inv * w1.z, v[c][7] * inv * w1.w);
+      o.x = pack_f16x2_sat(v[c][0] * inv * w0.x, v[c][1] * inv * w0.y, clip);
+      o.y = pack_f16x2_sat(v[c][2] * inv * w0.z, v[c][3] * inv * w0.w, clip);
+      o.z = pack_f16x2_sat(v[c][4] * inv * w1.x, v[c][5] * inv * w1.y, clip);
+      o.w = pack_f16x2_sat(v[c][6] * inv * w1.z, v[c][7] * inv * w1.w, clip);
       *reinterpret_cast<uint4*>(xn + static_cast<size_t>(m) * D + e) = o;
     }
   }
+  report_f16_clip(clip, status);
 }
 
 // One warp per row (rownorm.cuh).  With delta != null the residual add of the
 // preceding sub-layer happens here first: x += delta (written back), then the
 // norm of the updated row.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
-                               __half* __restrict__ y, int M, int D, float eps) {
+                               __half* __restrict__ y, int M, int D, float eps, uint32_t* __restrict__ status) {
   pdl_wait();
   pdl_launch_next();  // after the wait: at most one grid waits ahead
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
-  rownorm_row(x + static_cast<size_t>(m) * D, delta ? delta + static_cast<size_t>(m) * D : nullptr, true, w,
-              y + static_cast<size_t>(m) * D, D, eps, lane);
+  const bool clip = rownorm_row(x + static_cast<size_t>(m) * D, delta ? delta + static_cast<size_t>(m) * D : nullptr,
+                                true, w, y + static_cast<size_t>(m) * D, D, eps, lane);
+  report_f16_clip(clip, status);
 }
 
 // A wait on an mbarrier that nothing ever arrives on, bounded by limit_ns:
@@ -147,18 +150,19 @@ cudaError_t q4k_dequant_f16_launch(const uint8_t* blocks, int64_t nblocks, __hal
 }
 
 cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, const int32_t* lengths, int L, int M,
-                                 int D, const float* w, float eps, float* x, __half* xn, cudaStream_t st) {
+                                 int D, const float* w, float eps, float* x, __half* xn, uint32_t* status,
+                                 cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 256 != 0 || D > kMaxD) return cudaErrorInvalidValue;
   return launch_pdl(embed_rmsnorm_kernel, dim3((M + 7) / 8), dim3(256), 0, st, nullptr, 0, table, ids, lengths, L, M, D,
-                    w, eps, x, xn);
+                    w, eps, x, xn, status);
 }
 
 cudaError_t rmsnorm_launch(float* x, const float* delta, const float* w, __half* y, int M, int D, float eps,
-                           cudaStream_t st) {
+                           uint32_t* status, cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 128 != 0 || D > kMaxD) return cudaErrorInvalidValue;
-  return launch_pdl(rmsnorm_kernel, dim3((M + 7) / 8), dim3(256), 0, st, nullptr, 0, x, delta, w, y, M, D, eps);
+  return launch_pdl(rmsnorm_kernel, dim3((M + 7) / 8), dim3(256), 0, st, nullptr, 0, x, delta, w, y, M, D, eps, status);
 }
 
 }  // namespace wc

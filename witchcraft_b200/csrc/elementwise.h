@@ -15,12 +15,15 @@ cudaError_t q4k_dequant_f16_launch(const uint8_t* blocks, int64_t nblocks, __hal
 // x[m] = dequant(table row ids[m]) (id 0 for positions past a sequence's
 // valid length), xn[m] = f16(RMSNorm(x[m]) * w).  table: Q4_K [vocab][D/256].
 cudaError_t embed_rmsnorm_launch(const uint8_t* table, const uint32_t* ids, const int32_t* lengths, int L, int M,
-                                 int D, const float* w, float eps, float* x, __half* xn, cudaStream_t st);
+                                 int D, const float* w, float eps, float* x, __half* xn, uint32_t* status,
+                                 cudaStream_t st);
 
 // With delta != null first x[m] += delta[m] (the residual add, written back);
 // then y[m] = f16(x[m] / sqrt(mean(x[m]^2) + eps) * w), D % 128 == 0.
+// Both norms set kStatusF16Clipped in *status (may be null) when an output
+// value was clipped to the f16 range.
 cudaError_t rmsnorm_launch(float* x, const float* delta, const float* w, __half* y, int M, int D, float eps,
-                           cudaStream_t st);
+                           uint32_t* status, cudaStream_t st);
 
 // One warp waits on an mbarrier nobody arrives on, for at most limit_ns; the
 // timeout sets kStatusWaitTimeout in *status.

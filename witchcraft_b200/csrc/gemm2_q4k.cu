@@ -409,6 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ostage = 0;
     const uint32_t acc_empty_leader0 = map_to_rank(&acc_empty[0], 0);
     uint32_t it = 0;
+    bool clip = false;  // an f16 output value was clipped
     for (int tile = cid; tile < n_total; tile += ncl, ++it) {
       const uint32_t buf = it & 1;
 #ifdef WC_GEMM_TRACE
@@ -462,10 +463,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
                 uint4 o;
-                o.x = pack_f16x2_sat(v[8 * k], v[8 * k + 1]);
-                o.y = pack_f16x2_sat(v[8 * k + 2], v[8 * k + 3]);
-                o.z = pack_f16x2_sat(v[8 * k + 4], v[8 * k + 5]);
-                o.w = pack_f16x2_sat(v[8 * k + 6], v[8 * k + 7]);
+                o.x = pack_f16x2_sat(v[8 * k], v[8 * k + 1], clip);
+                o.y = pack_f16x2_sat(v[8 * k + 2], v[8 * k + 3], clip);
+                o.z = pack_f16x2_sat(v[8 * k + 4], v[8 * k + 5], clip);
+                o.w = pack_f16x2_sat(v[8 * k + 6], v[8 * k + 7], clip);
                 *reinterpret_cast<uint4*>(srow + (((4 * hc + k) ^ (lane & 7)) << 4)) = o;
               }
             }
@@ -493,6 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc_empty_leader0 + buf * 8);
     }
+    report_f16_clip(clip, p.status);
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
 

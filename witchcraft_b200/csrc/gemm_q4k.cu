@@ -218,6 +218,7 @@ __global__ void __launch_bounds__(320, 1)
     const int m = m0 + row;
     const bool acc_ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full, 0, p.status));
     tc_fence_after();
+    bool clip = false;  // an f16 output value was clipped
     if (acc_ok) {
       const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
       if (EPI == kEpiF16 || EPI == kEpiF32 || EPI == kEpiResid) {
@@ -232,10 +233,10 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
               for (int i = 0; i < 32; i += 8) {
                 uint4 o;
-                o.x = pack_f16x2_sat(v[i], v[i + 1]);
-                o.y = pack_f16x2_sat(v[i + 2], v[i + 3]);
-                o.z = pack_f16x2_sat(v[i + 4], v[i + 5]);
-                o.w = pack_f16x2_sat(v[i + 6], v[i + 7]);
+                o.x = pack_f16x2_sat(v[i], v[i + 1], clip);
+                o.y = pack_f16x2_sat(v[i + 2], v[i + 3], clip);
+                o.z = pack_f16x2_sat(v[i + 4], v[i + 5], clip);
+                o.w = pack_f16x2_sat(v[i + 6], v[i + 7], clip);
                 *reinterpret_cast<uint4*>(out + i) = o;
               }
             } else if (EPI == kEpiF32) {
@@ -269,10 +270,10 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
               uint4 o;
-              o.x = pack_f16x2_sat(gelu_tanh_fast(g[i]) * u[i], gelu_tanh_fast(g[i + 1]) * u[i + 1]);
-              o.y = pack_f16x2_sat(gelu_tanh_fast(g[i + 2]) * u[i + 2], gelu_tanh_fast(g[i + 3]) * u[i + 3]);
-              o.z = pack_f16x2_sat(gelu_tanh_fast(g[i + 4]) * u[i + 4], gelu_tanh_fast(g[i + 5]) * u[i + 5]);
-              o.w = pack_f16x2_sat(gelu_tanh_fast(g[i + 6]) * u[i + 6], gelu_tanh_fast(g[i + 7]) * u[i + 7]);
+              o.x = pack_f16x2_sat(gelu_tanh_fast(g[i]) * u[i], gelu_tanh_fast(g[i + 1]) * u[i + 1], clip);
+              o.y = pack_f16x2_sat(gelu_tanh_fast(g[i + 2]) * u[i + 2], gelu_tanh_fast(g[i + 3]) * u[i + 3], clip);
+              o.z = pack_f16x2_sat(gelu_tanh_fast(g[i + 4]) * u[i + 4], gelu_tanh_fast(g[i + 5]) * u[i + 5], clip);
+              o.w = pack_f16x2_sat(gelu_tanh_fast(g[i + 6]) * u[i + 6], gelu_tanh_fast(g[i + 7]) * u[i + 7], clip);
               *reinterpret_cast<uint4*>(out + i) = o;
             }
           }
@@ -312,6 +313,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     }
+    report_f16_clip(clip, p.status);
   }
 
   // ------------------------------------------------------------ teardown

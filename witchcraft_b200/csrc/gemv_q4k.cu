@@ -27,7 +27,7 @@ template <int EPI, int MT>
 __global__ void __launch_bounds__(kWarps * 32) gemv_q4k_kernel(const __half* __restrict__ X, int M, int K,
                                                                const uint8_t* __restrict__ W0,
                                                                const uint8_t* __restrict__ W1, void* __restrict__ out,
-                                                               int ldo) {
+                                                               int ldo, uint32_t* __restrict__ status) {
   constexpr int NMAT = EPI == kEpiGeGLU ? 2 : 1;
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* sX = smem;
@@ -43,12 +43,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q4k_kernel(const __half* __r
   gemv_issue_x<MT>(X, M, K, sX);
   gv_cp_async_wait_all();
   __syncthreads();
-  gemv_tile_compute<EPI, MT>(sX, M, K, sW, sRed, out, ldo, row0);
+  gemv_tile_compute<EPI, MT>(sX, M, K, sW, sRed, out, ldo, row0, status);
 }
 
 template <int EPI, int MT>
 cudaError_t launch(const __half* X, int M, int K, const uint8_t* W0, const uint8_t* W1, int N, void* out, int ldo,
-                   cudaStream_t st) {
+                   uint32_t* status, cudaStream_t st) {
   constexpr int NMAT = EPI == kEpiGeGLU ? 2 : 1;
   const size_t smem = gemv_sx_bytes(MT * 8, K) + gemv_sw_bytes(NMAT, K) + gemv_red_bytes(NMAT, MT * 8);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -63,15 +63,15 @@ cudaError_t launch(const __half* X, int M, int K, const uint8_t* W0, const uint8
     attr_set[dev] = true;
   }
   return launch_pdl(gemv_q4k_kernel<EPI, MT>, dim3(N / kRows), dim3(kWarps * 32), smem, st, nullptr, 0, X, M, K, W0,
-                    W1, out, ldo);
+                    W1, out, ldo, status);
 }
 
 template <int EPI>
 cudaError_t launch_mt(const __half* X, int M, int K, const uint8_t* W0, const uint8_t* W1, int N, void* out, int ldo,
-                      cudaStream_t st) {
-  if (M <= 8) return launch<EPI, 1>(X, M, K, W0, W1, N, out, ldo, st);
-  if (M <= 16) return launch<EPI, 2>(X, M, K, W0, W1, N, out, ldo, st);
-  return launch<EPI, 4>(X, M, K, W0, W1, N, out, ldo, st);
+                      uint32_t* status, cudaStream_t st) {
+  if (M <= 8) return launch<EPI, 1>(X, M, K, W0, W1, N, out, ldo, status, st);
+  if (M <= 16) return launch<EPI, 2>(X, M, K, W0, W1, N, out, ldo, status, st);
+  return launch<EPI, 4>(X, M, K, W0, W1, N, out, ldo, status, st);
 }
 
 }  // namespace
@@ -82,11 +82,11 @@ bool gemv_q4k_supports(int epi, int M, int N, int K) {
 }
 
 cudaError_t gemv_q4k_launch(int epi, const __half* X, int M, int K, const uint8_t* W0, const uint8_t* W1, int N,
-                            void* out, int ldo, cudaStream_t st) {
+                            void* out, int ldo, uint32_t* status, cudaStream_t st) {
   switch (epi) {
-    case kEpiF16: return launch_mt<kEpiF16>(X, M, K, W0, W1, N, out, ldo, st);
-    case kEpiF32: return launch_mt<kEpiF32>(X, M, K, W0, W1, N, out, ldo, st);
-    case kEpiGeGLU: return launch_mt<kEpiGeGLU>(X, M, K, W0, W1, N, out, ldo, st);
+    case kEpiF16: return launch_mt<kEpiF16>(X, M, K, W0, W1, N, out, ldo, status, st);
+    case kEpiF32: return launch_mt<kEpiF32>(X, M, K, W0, W1, N, out, ldo, status, st);
+    case kEpiGeGLU: return launch_mt<kEpiGeGLU>(X, M, K, W0, W1, N, out, ldo, status, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -13,8 +13,9 @@ constexpr int kGemvMaxRows = 32;
 // K <= 2048.
 bool gemv_q4k_supports(int epi, int M, int N, int K);
 
-// X f16 [M][K] (row stride K); W raw Q4_K rows; out [M][ldo].
+// X f16 [M][K] (row stride K); W raw Q4_K rows; out [M][ldo].  f16 outputs
+// clipped to the f16 range set kStatusF16Clipped in *status (may be null).
 cudaError_t gemv_q4k_launch(int epi, const __half* X, int M, int K, const uint8_t* W0, const uint8_t* W1, int N,
-                            void* out, int ldo, cudaStream_t st);
+                            void* out, int ldo, uint32_t* status, cudaStream_t st);
 
 }  // namespace wc

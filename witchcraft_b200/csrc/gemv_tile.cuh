@@ -100,7 +100,8 @@ __device__ __forceinline__ void gemv_issue_x(const __half* __restrict__ X, int M
 // with sX, sW and sRed.
 template <int EPI, int MT>
 __device__ __forceinline__ void gemv_tile_compute(const uint8_t* sX, int M, int K, const uint8_t* sW, float* sRed,
-                                                  void* __restrict__ out, int ldo, int row0) {
+                                                  void* __restrict__ out, int ldo, int row0,
+                                                  uint32_t* __restrict__ status) {
   constexpr int NMAT = EPI == kEpiGeGLU ? 2 : 1;
   constexpr int TOK = MT * 8;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -169,6 +170,7 @@ __device__ __forceinline__ void gemv_tile_compute(const uint8_t* sX, int M, int 
         sRed[((warp * NMAT + m) * kGemvRows + f) * TOK + tok] = acc[m][t][e];
       }
   __syncthreads();
+  bool clip = false;  // an f16 output value was clipped
   for (int i = tid; i < kGemvRows * M; i += blockDim.x) {
     const int f = i % kGemvRows, tok = i / kGemvRows;
     float v[NMAT];
@@ -182,13 +184,16 @@ __device__ __forceinline__ void gemv_tile_compute(const uint8_t* sX, int M, int 
     const size_t o = static_cast<size_t>(tok) * ldo + row0 + f;
     if (EPI == kEpiGeGLU) {
       const float h = gelu_tanh_fast(v[0]) * v[NMAT - 1];
+      clip |= f16_clips(h);
       reinterpret_cast<__half*>(out)[o] = __float2half_rn(fminf(fmaxf(h, -65504.f), 65504.f));
     } else if (EPI == kEpiF16) {
+      clip |= f16_clips(v[0]);
       reinterpret_cast<__half*>(out)[o] = __float2half_rn(fminf(fmaxf(v[0], -65504.f), 65504.f));
     } else {
       reinterpret_cast<float*>(out)[o] = v[0];
     }
   }
+  report_f16_clip(clip, status);
   __syncthreads();
 }
 

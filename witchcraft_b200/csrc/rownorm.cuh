@@ -17,7 +17,7 @@ __device__ __forceinline__ float rownorm_warp_sum(float v) {
 // Lane owns float4 groups lane + 32 g, g < D / 128.  v = x (+ delta), written
 // back to x when write_x; y = f16(v * (1 / sqrt(mean(v^2) + eps)) * w).  y may
 // point to global or shared memory (8-byte aligned row).
-__device__ __forceinline__ void rownorm_row(float* __restrict__ x, const float* __restrict__ delta, bool write_x,
+__device__ __forceinline__ bool rownorm_row(float* __restrict__ x, const float* __restrict__ delta, bool write_x,
                                             const float* __restrict__ w, __half* __restrict__ y, int D, float eps,
                                             int lane) {
   const int ng = D / 128;
@@ -46,16 +46,18 @@ __device__ __forceinline__ void rownorm_row(float* __restrict__ x, const float* 
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
   uint2* yr = reinterpret_cast<uint2*>(y);
   const float4* wr = reinterpret_cast<const float4*>(w);
+  bool clip = false;
 #pragma unroll
   for (int g = 0; g < kRowNormMaxD / 128; ++g) {
     if (g < ng) {
       const float4 ww = wr[lane + 32 * g];
       uint2 o;
-      o.x = pack_f16x2_sat(v[g].x * inv * ww.x, v[g].y * inv * ww.y);
-      o.y = pack_f16x2_sat(v[g].z * inv * ww.z, v[g].w * inv * ww.w);
+      o.x = pack_f16x2_sat(v[g].x * inv * ww.x, v[g].y * inv * ww.y, clip);
+      o.y = pack_f16x2_sat(v[g].z * inv * ww.z, v[g].w * inv * ww.w, clip);
       yr[lane + 32 * g] = o;
     }
   }
+  return clip;  // whether an output value was clipped to the f16 range
 }
 
 }  // namespace wc

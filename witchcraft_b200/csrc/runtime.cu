@@ -134,6 +134,9 @@ struct LayerW {
   // The same matrices dequantised once to f16 [N][K] (the large-M GEMMs)
   __half *h_qkv, *h_o, *h_wi0, *h_wi1, *h_wo;
   CUtensorMap tmh_qkv, tmh_o, tmh_wi0, tmh_wi1, tmh_wo;
+  // Raw Q4_K rows with the 2-SM kernel's box, for its fused-dequant variant
+  // (handles created with WC_F16_WEIGHTS=0)
+  CUtensorMap tmq2_qkv, tmq2_o, tmq2_wi0, tmq2_wi1, tmq2_wo;
 };
 
 // Rows from which the 2-SM persistent GEMM replaces the 1-SM kernel.
@@ -162,6 +165,9 @@ struct wc_t5 {
   int bn_qkv = 0, bn_o = 0, bn_wi = 0, bn_wo = 0;
   uint8_t* arena = nullptr;  // all weights, one allocation
   __half* arena_f16 = nullptr;  // the layer matrices dequantised to f16, one allocation
+  // Large-M GEMMs on the resident f16 copies (default) or, with
+  // WC_F16_WEIGHTS=0 at create time, dequantising the Q4_K rows in the kernel
+  bool f16_weights = true;
   uint8_t* embed = nullptr;
   uint8_t* proj = nullptr;
   float* final_ln = nullptr;
@@ -315,7 +321,7 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
                cudaStream_t st, const __half* a_ptr, const uint8_t* w0_ptr, const uint8_t* w1_ptr) {
   const int feat = epi == kEpiGeGLU ? N / 2 : N;
   if (gemv_q4k_supports(epi, M, feat, K)) {
-    cudaError_t e = gemv_q4k_launch(epi, a_ptr, M, K, w0_ptr, w1_ptr, feat, out, ldo, st);
+    cudaError_t e = gemv_q4k_launch(epi, a_ptr, M, K, w0_ptr, w1_ptr, feat, out, ldo, h->d_status, st);
     return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
   }
   if (M >= kGemm2MinRows && gemm2_q4k_supports(epi, M, N, K)) {
@@ -329,7 +335,7 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
     CUtensorMap tm_out;
     if (!make_out_map(&tm_out, out, M, ldo, epi == kEpiF32 || epi == kEpiResid))
       return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a GEMM output");
-    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, device_sm_count(h->device), st, true);
+    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, device_sm_count(h->device), st, h->f16_weights);
     return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
   }
   return gemm(h, epi, bn, a, w0, w1, M, N, K, out, ldo, st);
@@ -351,7 +357,11 @@ int check_status(wc_t5* h, cudaStream_t st) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_fail(h, e, "synchronising the forward");
   if (s & kStatusWaitTimeout) return fail(h, WC_E_TIMEOUT, "an in-kernel wait timed out");
-  if (s) return fail(h, WC_E_CUDA, "kernel reported status " + std::to_string(s));
+  if (s & ~kStatusF16Clipped) return fail(h, WC_E_CUDA, "kernel reported status " + std::to_string(s));
+  if (s & kStatusF16Clipped)
+    return fail(h, WC_W_F16_CLIPPED,
+                "an f16 activation exceeded the f16 range and was clipped to +-65504; the outputs may deviate "
+                "from the f32 reference");
   return WC_OK;
 }
 
@@ -644,7 +654,12 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
          make_q4k_map(&w.tm_o, w.o, D, I, gemm_q4k_w_box_rows(kEpiF32, h->bn_o)) &&
          make_q4k_map(&w.tm_wi0, w.wi0, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
          make_q4k_map(&w.tm_wi1, w.wi1, F, D, gemm_q4k_w_box_rows(kEpiGeGLU, h->bn_wi)) &&
-         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiF32, h->bn_wo));
+         make_q4k_map(&w.tm_wo, w.wo, D, F, gemm_q4k_w_box_rows(kEpiF32, h->bn_wo)) &&
+         make_q4k_map(&w.tmq2_qkv, w.qkv, 3 * I, D, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tmq2_o, w.o, D, I, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tmq2_wi0, w.wi0, F, D, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tmq2_wi1, w.wi1, F, D, kGemm2WBoxRows) &&
+         make_q4k_map(&w.tmq2_wo, w.wo, D, F, kGemm2WBoxRows);
   }
   if (!ok) {
     wc_t5_destroy(h);
@@ -654,6 +669,10 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
   // reference dequantises its Q4_K weights once at load, and so does this,
   // with the rounding to f16 the fused-dequant kernels apply to their operands.
   {
+    const char* fw = getenv("WC_F16_WEIGHTS");
+    h->f16_weights = !(fw && fw[0] == '0' && fw[1] == 0);
+  }
+  if (h->f16_weights) {
     const int64_t per_layer = (3 * static_cast<int64_t>(I) * D + static_cast<int64_t>(D) * I +
                                2 * static_cast<int64_t>(F) * D + static_cast<int64_t>(D) * F);
     if ((e = cudaMalloc(&h->arena_f16, per_layer * cfg.num_layers * sizeof(__half))) != cudaSuccess) {
@@ -978,6 +997,16 @@ extern "C" int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, c
   return check_status(h, cs);
 }
 
+extern "C" void* wc_host_alloc(size_t bytes) {
+  void* p = nullptr;
+  if (bytes == 0 || cudaHostAlloc(&p, bytes, cudaHostAllocPortable) != cudaSuccess) return nullptr;
+  return p;
+}
+
+extern "C" void wc_host_free(void* p) {
+  if (p) cudaFreeHost(p);
+}
+
 extern "C" int wc_t5_forward_many_device(wc_t5* h, int n, const uint32_t* const* d_ids,
                                          const int32_t* const* d_lengths, const int* B, const int* L,
                                          float* const* d_out, float* const* d_norms, void* stream) {
@@ -1080,7 +1109,7 @@ extern "C" int wc_gemm_q4k(const void* d_x, int M, int K, const void* d_w, const
   if (gemv_q4k_supports(epilogue, M, N, K))
     return gemv_q4k_launch(epilogue, static_cast<const __half*>(d_x), M, K, static_cast<const uint8_t*>(d_w),
                            static_cast<const uint8_t*>(epilogue == kEpiGeGLU ? d_w_up : d_w), N, d_out, N,
-                           static_cast<cudaStream_t>(stream)) == cudaSuccess
+                           nullptr, static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? WC_OK
                : WC_E_CUDA;
   if (M >= kGemm2MinRows && gemm2_q4k_supports(epilogue, M, tile_n, K)) {
@@ -1276,30 +1305,30 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
   void* res_out = fused_res ? static_cast<void*>(x) : static_cast<void*>(qkv);
   const float* res_delta = fused_res ? nullptr : reinterpret_cast<const float*>(qkv);
   cudaError_t e;
-  if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, x, xn, st)) !=
+  if ((e = embed_rmsnorm_launch(h->embed, ids, lengths, L, M, D, h->layers[0].ln0, c.eps, x, xn, h->d_status, st)) !=
       cudaSuccess)
     return cuda_fail(h, e, "embedding launch");
   FWD_MARK();
   int rc;
   for (int l = 0; l < c.num_layers; ++l) {
     LayerW& w = h->layers[l];
-    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, w.tmh_qkv, w.tmh_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
+    if ((rc = layer_gemm(h, kEpiF16, h->bn_qkv, tm_xn, w.tm_qkv, w.tm_qkv, h->f16_weights ? w.tmh_qkv : w.tmq2_qkv, h->f16_weights ? w.tmh_qkv : w.tmq2_qkv, M, 3 * I, D, qkv, 3 * I, st, xn, w.qkv, w.qkv))) return rc;
     FWD_MARK();
     e = attention_small_supports(L) ? attention_small_launch(qkv, att, lengths, B, L, H, h->rel_bias, h->bt, st)
                                     : attention_tc_launch(tm_qkv, att, lengths, B, L, H, h->rel_bias, h->bt,
                                                           h->d_status, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "attention launch");
     FWD_MARK();
-    if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, w.tmh_o, w.tmh_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, h->f16_weights ? w.tmh_o : w.tmq2_o, h->f16_weights ? w.tmh_o : w.tmq2_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
     FWD_MARK();
-    if ((e = rmsnorm_launch(x, res_delta, w.ln1, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    if ((e = rmsnorm_launch(x, res_delta, w.ln1, xn, M, D, c.eps, h->d_status, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
     FWD_MARK();
-    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, w.tmh_wi0, w.tmh_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
+    if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, h->f16_weights ? w.tmh_wi0 : w.tmq2_wi0, h->f16_weights ? w.tmh_wi1 : w.tmq2_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
     FWD_MARK();
-    if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, w.tmh_wo, w.tmh_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, h->f16_weights ? w.tmh_wo : w.tmq2_wo, h->f16_weights ? w.tmh_wo : w.tmq2_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo))) return rc;
     FWD_MARK();
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
-    if ((e = rmsnorm_launch(x, res_delta, next_ln, xn, M, D, c.eps, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    if ((e = rmsnorm_launch(x, res_delta, next_ln, xn, M, D, c.eps, h->d_status, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
     FWD_MARK();
   }
   return gemm(h, kEpiProj, 128, tm_xn, h->tm_proj, h->tm_proj, M, h->d_proj, D, out, h->d_proj, st, norms, outn,

@@ -89,27 +89,43 @@ class Gatherer:
     def __iter__(self) -> Iterator[tuple[str, np.ndarray, list[int]]]:
         return self
 
+    def next_group(self) -> list[tuple[str, np.ndarray, list[int]]]:
+        """The next up to `group_docs` documents' results, in input order
+        (empty at the end)."""
+        group = []
+        for d in self._docs:
+            group.append(d)
+            if len(group) == self._group:
+                break
+        if not group:
+            return []
+        results = self._embedder.embed_ids_batch([d.ids for d in group], [d.offsets for d in group],
+                                                 max_batch_tokens=self._max_tokens)
+        return [(d.hash, emb[0], chunk_counts(kept, d.lens)) for d, (emb, kept) in zip(group, results)]
+
     def __next__(self) -> tuple[str, np.ndarray, list[int]]:
         if not self._ready:
-            group = []
-            for d in self._docs:
-                group.append(d)
-                if len(group) == self._group:
-                    break
-            if not group:
+            self._ready = self.next_group()
+            if not self._ready:
                 raise StopIteration
-            results = self._embedder.embed_ids_batch([d.ids for d in group], [d.offsets for d in group],
-                                                     max_batch_tokens=self._max_tokens)
-            for d, (emb, kept) in zip(group, results):
-                self._ready.append((d.hash, emb[0], chunk_counts(kept, d.lens)))
             self._ready.reverse()
         return self._ready.pop()
 
 
-def embed_chunks(documents: Iterable[Document], embedder, pack=None, **kw):
+def embed_chunks(documents: Iterable[Document], embedder, pack=None, pack_many=None, **kw):
     """The reference's embed_chunks loop without the database: yields
-    (hash, payload, counts string) per document, payload = pack(embeddings)
-    (the packed codec bytes, `add_chunk`'s blob) or the f32 rows when pack
-    is None."""
-    for h, emb, counts in Gatherer(documents, embedder, **kw):
-        yield h, (pack(emb) if pack is not None else emb), ",".join(str(c) for c in counts)
+    (hash, payload, counts string) per document, in input order.  The payload
+    is `add_chunk`'s blob: with pack_many (e.g. `codec.pack_many`, one
+    wc_pack_embeddings call per document group) or pack (one document at a
+    time) the packed codec bytes, otherwise the f32 rows."""
+    g = Gatherer(documents, embedder, **kw)
+    while True:
+        group = g.next_group()
+        if not group:
+            return
+        if pack_many is not None:
+            payloads = pack_many([emb for _, emb, _ in group])
+        else:
+            payloads = [pack(emb) if pack is not None else emb for _, emb, _ in group]
+        for (h, _, counts), p in zip(group, payloads):
+            yield h, p, ",".join(str(c) for c in counts)

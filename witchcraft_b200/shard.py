@@ -53,13 +53,20 @@ def plan_batches(lengths: np.ndarray, max_tokens: int = 16384) -> list[Batch]:
     return out
 
 
-def assign_batches(batches: list[Batch], world: int) -> list[list[int]]:
-    """Greedy longest-processing-time assignment of batches to `world` ranks
-    by padded token count.  Returns the batch indices of each rank."""
+def lpt_assign(costs, world: int) -> list[list[int]]:
+    """Greedy longest-processing-time assignment of items with the given
+    costs to `world` workers (largest first, each to the least-loaded worker;
+    ties to the lowest worker index).  Returns the item indices per worker."""
     loads = np.zeros(world, np.int64)
     owners: list[list[int]] = [[] for _ in range(world)]
-    for i in sorted(range(len(batches)), key=lambda i: -batches[i].padded_tokens):
+    for i in sorted(range(len(costs)), key=lambda i: -costs[i]):
         r = int(np.argmin(loads))
         owners[r].append(i)
-        loads[r] += batches[i].padded_tokens
+        loads[r] += costs[i]
     return owners
+
+
+def assign_batches(batches: list[Batch], world: int) -> list[list[int]]:
+    """LPT assignment of batches to `world` ranks by padded token count.
+    Returns the batch indices of each rank."""
+    return lpt_assign([b.padded_tokens for b in batches], world)

@@ -191,10 +191,13 @@ class SyntheticModel:
 
 
 def make_synthetic_model(cfg: T5Config | None = None, seed: int = 0, std: float = 0.02,
-                         bias_std: float = 0.1, norm_weight: float = 1.0) -> SyntheticModel:
+                         bias_std: float = 0.1, norm_weight: float = 1.0,
+                         ff_norm_weight: float | None = None) -> SyntheticModel:
     """Random-init N(0, std) weights quantized to Q4_K, RMSNorm weights
-    `norm_weight`, relative-attention bias N(0, bias_std); tensor names as in
-    the reference checkpoint (`src/quantized_t5.rs:514-516,582-590,639-646,682-690`)."""
+    `norm_weight` (the feed-forward sub-layers' norms `ff_norm_weight` when
+    given: a large value drives the gated-GELU output past the f16 range),
+    relative-attention bias N(0, bias_std); tensor names as in the reference
+    checkpoint (`src/quantized_t5.rs:514-516,582-590,639-646,682-690`)."""
     cfg = cfg or T5Config()
     rng = np.random.default_rng(seed)
     D, F, inner, H = cfg.d_model, cfg.d_ff, cfg.num_heads * cfg.d_kv, cfg.num_heads
@@ -225,7 +228,8 @@ def make_synthetic_model(cfg: T5Config | None = None, seed: int = 0, std: float 
         add_q4k(f"{p}.1.DenseReluDense.wi_0.weight", F, D)
         add_q4k(f"{p}.1.DenseReluDense.wi_1.weight", F, D)
         add_q4k(f"{p}.1.DenseReluDense.wo.weight", D, F)
-        add_f32(f"{p}.1.layer_norm.weight", np.full(D, norm_weight, np.float32))
+        add_f32(f"{p}.1.layer_norm.weight",
+                np.full(D, norm_weight if ff_norm_weight is None else ff_norm_weight, np.float32))
     add_f32("encoder.final_layer_norm.weight", np.full(D, norm_weight, np.float32))
     add_q4k("linear.weight", cfg.d_proj, D)
     m.gguf = write_gguf(tensors)

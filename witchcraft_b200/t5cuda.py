@@ -89,18 +89,28 @@ class T5EncoderModel:
         """[(ids [B, L] u32, lengths [B] or None)] -> [raw [B, L, 128]] (and norms),
         pipelined through wc_t5_forward_many (copies overlap the compute when
         the arrays are page-locked)."""
+        ids = [np.ascontiguousarray(np.atleast_2d(b[0]), dtype=np.uint32) for b in batches]
+        outs = [np.empty((a.shape[0], a.shape[1], self.d_proj), np.float32) for a in ids]
+        norms = [np.empty(a.shape, np.float32) for a in ids] if with_norms else None
+        self.forward_many_into(batches, outs, norms)
+        return (outs, norms) if with_norms else outs
+
+    def forward_many_into(self, batches, outs, norms=None) -> None:
+        """forward_many writing into caller-owned arrays: outs[i] f32 [B, L, 128]
+        (C-contiguous, e.g. views of page-locked buffers), norms[i] f32 [B, L] or
+        norms None."""
         n = len(batches)
         ids = [np.ascontiguousarray(np.atleast_2d(b[0]), dtype=np.uint32) for b in batches]
         lens = [None if b[1] is None else np.ascontiguousarray(b[1], dtype=np.int32) for b in batches]
-        outs = [np.empty((a.shape[0], a.shape[1], self.d_proj), np.float32) for a in ids]
-        norms = [np.empty(a.shape, np.float32) for a in ids] if with_norms else None
+        for a, o in zip(ids, outs):
+            if o.dtype != np.float32 or not o.flags["C_CONTIGUOUS"] or o.size < a.size * self.d_proj:
+                raise ValueError("output array must be C-contiguous f32 with B * L * 128 elements")
         vp = ctypes.c_void_p
         arr = lambda xs: (vp * n)(*[vp(x.ctypes.data) if x is not None else None for x in xs])  # noqa: E731
         Bs = (ctypes.c_int * n)(*[a.shape[0] for a in ids])
         Ls = (ctypes.c_int * n)(*[a.shape[1] for a in ids])
         check(lib().wc_t5_forward_many(self._h, n, arr(ids), arr(lens), Bs, Ls, arr(outs),
                                        arr(norms) if norms is not None else None), self._h)
-        return (outs, norms) if with_norms else outs
 
     def forward_device(self, d_ids: int, d_lengths: int, B: int, L: int, d_out: int, d_norms: int | None = None,
                        d_outn: int | None = None, stream: int | None = None) -> None:
@@ -124,6 +134,35 @@ class T5EncoderModel:
 
     def sync(self, stream: int | None = None) -> None:
         check(lib().wc_t5_sync(self._h, ctypes.c_void_p(stream) if stream else None), self._h)
+
+
+class HostBuffer:
+    """Page-locked host memory from the library (wc_host_alloc), viewed as a
+    numpy array; freed by close() or when collected."""
+
+    def __init__(self, nbytes: int):
+        self._p = lib().wc_host_alloc(int(nbytes))
+        if not self._p:
+            raise MemoryError(f"wc_host_alloc({nbytes}) failed")
+        self.nbytes = int(nbytes)
+
+    def array(self, shape, dtype=np.float32, offset: int = 0) -> np.ndarray:
+        n = int(np.prod(shape)) * np.dtype(dtype).itemsize
+        if offset + n > self.nbytes:
+            raise ValueError("view past the end of the buffer")
+        raw = (ctypes.c_char * n).from_address(self._p + offset)
+        return np.frombuffer(raw, dtype=dtype).reshape(shape)
+
+    def close(self) -> None:
+        if getattr(self, "_p", None):
+            lib().wc_host_free(self._p)
+            self._p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class T5ModelBuilder:
@@ -225,6 +264,7 @@ class Embedder:
             for start, end in _windows(len(ids)):
                 wins.append(_Window(d, start, ids[start:end]))
         wins.sort(key=lambda w: len(w.ids))
+        plan = []  # (windows, padded ids, lengths) per batch
         i = 0
         while i < len(wins):
             L = len(wins[i].ids)
@@ -239,8 +279,14 @@ class Embedder:
             for b, w in enumerate(batch):
                 ids[b, :len(w.ids)] = w.ids
                 lens[b] = len(w.ids)
-            out = self.model.forward(ids, lens)
+            plan.append((batch, ids, lens))
+            i = j
+        if hasattr(self.model, "forward_many"):
+            # one pipelined call for all batches (copies overlap the compute)
+            outs = self.model.forward_many([(ids, lens) for _, ids, lens in plan])
+        else:
+            outs = [self.model.forward(ids, lens) for _, ids, lens in plan]
+        for (batch, _, _), out in zip(plan, outs):
             for b, w in enumerate(batch):
                 accums[w.doc][w.start:w.start + len(w.ids)] += out[b, :len(w.ids)]
-            i = j
         return [_finish(a, None if offsets is None else offsets[d]) for d, a in enumerate(accums)]
