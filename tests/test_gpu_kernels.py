@@ -192,8 +192,8 @@ def _attention_torch(qkv, B, L, H, lengths, bias_tab):
                                          # L <= 64: the mma.sync kernel of short batches
                                          (4, 32, [32, 17, 1, 5]), (2, 64, [64, 40]), (3, 17, [17, 9, 16]),
                                          (2, 2, [2, 1]), (2, 33, [33, 20]), (3, 31, [0, 31, 7]),
-                                         # 65 <= L <= 1024: the two-tile kernel (pairs of query tiles of
-                                         # one head, or the last tile of two heads when the count is odd)
+                                         # L > 64: the tcgen05 kernel with odd tile counts, an empty
+                                         # sequence and the 1024 / 1025 sizes
                                          (3, 300, [0, 300, 129]), (2, 384, [300, 384]), (1, 1024, [1024]),
                                          (5, 129, [129, 128, 127, 64, 65]), (2, 1025, [1025, 700])])
 def test_attention_matches_oracle(B, L, lengths):
@@ -214,8 +214,8 @@ def test_attention_matches_oracle(B, L, lengths):
 
 @pytest.mark.parametrize("H", [2, 6, 3, 16])
 def test_attention_head_counts(H):
-    """Even head counts up to 16 take the two-tile kernel; an odd count the
-    single-tile one.  Both against the fp32 torch reference."""
+    """Head counts from 2 to 16, odd and even, against the fp32 torch
+    reference; rows of wholly padded query tiles are zero."""
     B, L = 3, 260
     lengths = [260, 131, 77]
     qkv = torch.randn(B * L, 3 * H * 64, generator=torch.Generator().manual_seed(H)).to(torch.float16).cuda()

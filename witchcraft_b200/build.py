@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libwc_t5cuda.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 
-CUDA_SOURCES = ["gemm_q4k.cu", "gemm2_q4k.cu", "gemv_q4k.cu", "attention_tc.cu", "attention_fa.cu", "attention_small.cu", "elementwise.cu", "runtime.cu", "codec.cu", "index.cu", "query.cu"]
+CUDA_SOURCES = ["gemm_q4k.cu", "gemm2_q4k.cu", "gemv_q4k.cu", "attention_tc.cu", "attention_small.cu", "elementwise.cu", "runtime.cu", "codec.cu", "index.cu", "query.cu"]
 CXX_SOURCES = ["t5_host.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

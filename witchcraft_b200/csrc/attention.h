@@ -22,13 +22,6 @@ struct BucketThresholds {
 cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const int32_t* lengths, int B, int L, int H,
                                 const float* bias_tab, const BucketThresholds& bt, uint32_t* status, cudaStream_t st);
 
-// Padded lengths 65..1024, an even head count <= 16 and B <= 1024: the
-// two-tile ping-pong kernel (attention_fa.cu); attention_tc_launch uses it
-// for those shapes (WC_ATTN_V1=1 keeps the single-tile kernel).
-bool attention_fa_supports(int B, int L, int H, int num_buckets);
-cudaError_t attention_fa_launch(const CUtensorMap& tm_qkv, __half* out, const int32_t* lengths, int B, int L, int H,
-                                const float* bias_tab, const BucketThresholds& bt, uint32_t* status, cudaStream_t st);
-
 // Short padded batches (1 <= L <= 64, the query path): mma.sync kernel over
 // the raw QKV pointer, one CTA per (sequence, head).
 bool attention_small_supports(int L);

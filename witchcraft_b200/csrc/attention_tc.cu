@@ -585,12 +585,6 @@ cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const in
                                 const float* bias_tab, const BucketThresholds& bt, uint32_t* status,
                                 cudaStream_t st) {
   if (B <= 0 || L <= 0) return cudaSuccess;
-  static const bool v1 = [] {
-    const char* v = getenv("WC_ATTN_V1");
-    return v && v[0] == '1' && v[1] == 0;
-  }();
-  if (!v1 && attention_fa_supports(B, L, H, 2 * bt.half))
-    return attention_fa_launch(tm_qkv, out, lengths, B, L, H, bias_tab, bt, status, st);
   if (L > kMaxL || 2 * bt.half > 64 || H <= 0 || H > kMaxHeads) return cudaErrorInvalidValue;
   const int64_t n_items = static_cast<int64_t>((L + kQ - 1) / kQ) * B * H;
   if (n_items > INT32_MAX || static_cast<int64_t>(B) * L > INT32_MAX) return cudaErrorInvalidValue;

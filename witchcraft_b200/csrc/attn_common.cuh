@@ -1,5 +1,4 @@
-// Device helpers shared by the tcgen05 attention kernels (attention_tc.cu,
-// attention_fa.cu): TMEM stores and unwaited loads, the MUFU exponential,
+// Device helpers of the tcgen05 attention kernel (attention_tc.cu): TMEM stores and unwaited loads, the MUFU exponential,
 // the MN-major shared-memory descriptor of the V operand and the bucket
 // lookup from monotone thresholds.
 #pragma once
