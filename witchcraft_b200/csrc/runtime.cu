@@ -257,7 +257,9 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 int ensure_workspace(wc_t5* h, int64_t rows, int B) {
   if (rows <= h->cap_rows && B <= h->cap_b) return WC_OK;
   const int64_t cap = std::max<int64_t>((rows + 127) / 128 * 128, h->cap_rows);
-  const int capb = std::max(B, h->cap_b);
+  // B <= rows always (L >= 1): size the lengths for `cap` rows so a batch of
+  // many short rows never reallocates the workspace on its own
+  const int capb = static_cast<int>(std::max<int64_t>({cap, static_cast<int64_t>(B), h->cap_b}));
   free_workspace(h);
   const int D = h->cfg.d_model, F = h->cfg.d_ff, I = h->inner, P = h->d_proj;
   size_t off = 0;
@@ -844,7 +846,7 @@ int ensure_io(wc_t5* h, int64_t rows, int B) {
     h->io = nullptr;
   }
   const int64_t cap = std::max<int64_t>((rows + 127) / 128 * 128, h->io_rows);
-  const int capb = std::max(B, h->io_b);
+  const int capb = static_cast<int>(std::max<int64_t>({cap, static_cast<int64_t>(B), h->io_b}));
   const size_t P = h->d_proj;
   size_t off = 0, o_ids[2], o_len[2], o_out[2], o_norms[2];
   for (int i = 0; i < 2; ++i) {
@@ -963,8 +965,14 @@ extern "C" int wc_t5_forward_many(wc_t5* h, int n, const uint32_t* const* ids, c
     // compute: inputs of batch i landed; d_out of set s read out (batch i - 2)
     if ((e = cudaStreamWaitEvent(fs, h->ev_in[s], 0)) != cudaSuccess) break;
     if (i >= 2 && (e = cudaStreamWaitEvent(fs, h->ev_out[s], 0)) != cudaSuccess) break;
-    if (fs == cs)
+    // Bulk calls (two lanes) launch their small batches eagerly: a one-off
+    // shape would pay a graph capture and instantiation (tens of ms when
+    // another process shares the driver) and never replay it.
+    if (fs == cs && !two_lanes)
       rc = forward_cached(h, h->io_ids[s], h->io_len[s], B[i], L[i], h->io_out[s], nrm ? h->io_norms[s] : nullptr,
+                          nullptr, cs);
+    else if (fs == cs)
+      rc = forward_device(h, h->io_ids[s], h->io_len[s], B[i], L[i], h->io_out[s], nrm ? h->io_norms[s] : nullptr,
                           nullptr, cs);
     else
       rc = forward_on(h, h->lane_x, h->lane_xn, h->lane_qkv, h->lane_att, h->lane_h, h->lane_tm_xn,
@@ -1041,8 +1049,10 @@ extern "C" int wc_t5_forward_many_device(wc_t5* h, int n, const uint32_t* const*
   if (e != cudaSuccess) return cuda_fail(h, e, "lane fork");
   for (int i = 0; i < n && rc == WC_OK; ++i) {
     float* nrm = d_norms ? d_norms[i] : nullptr;
-    if (!two_lanes || (i & 1) == 0)
+    if (!two_lanes)
       rc = forward_cached(h, d_ids[i], d_lengths[i], B[i], L[i], d_out[i], nrm, nullptr, cs);
+    else if ((i & 1) == 0)  // bulk: no graph capture of one-off shapes
+      rc = forward_device(h, d_ids[i], d_lengths[i], B[i], L[i], d_out[i], nrm, nullptr, cs);
     else
       rc = forward_on(h, h->lane_x, h->lane_xn, h->lane_qkv, h->lane_att, h->lane_h, h->lane_tm_xn,
                       h->lane_tm_att, h->lane_tm_h, d_ids[i], d_lengths[i], B[i], L[i], d_out[i], nrm, nullptr,
