@@ -866,7 +866,7 @@ def profile_kernel(name: str, m: int, launches: int = 5, fused_q4k: bool = False
         bt = torch.randn(32, H, device="cuda") * 0.1
         f = lambda: check(l.wc_attention(P(qkv), B, L, H, P(lens), P(bt), 32, 128, P(out), None))  # noqa: E731
     else:
-        K, N, epi = {"geglu": (768, 2048, 1), "qkv": (768, 2304, 0), "wo": (2048, 768, 2)}[name]
+        K, N, epi = {"geglu": (768, 2048, 1), "qkv": (768, 2304, 0), "wo": (2048, 768, 3), "o": (768, 768, 3)}[name]
         w, wu = wq(N, K), (wq(N, K) if epi == 1 else None)
         x = torch.randn(m, K, device="cuda").half()
         y = torch.zeros(m, N, device="cuda", dtype=torch.float16 if epi in (0, 1) else torch.float32)
@@ -892,7 +892,7 @@ def main():
                     help="skip the whole-corpus (strong scaling) encode")
     ap.add_argument("--lanes", type=int, choices=[1, 2], default=2,
                     help="device-resident leg: encoder handles on their own streams taking alternate batches")
-    ap.add_argument("--profile-kernel", choices=["geglu", "qkv", "wo", "attention"], default=None,
+    ap.add_argument("--profile-kernel", choices=["geglu", "qkv", "wo", "o", "attention"], default=None,
                     help="only launch one kernel a few times (for ncu)")
     ap.add_argument("--m", type=int, default=16384, help="GEMM rows for --profile-kernel")
     ap.add_argument("--fused-q4k", action="store_true", help="--profile-kernel: the Q4_K-dequantising GEMM")
