@@ -62,13 +62,14 @@ constexpr int kOffOut = kOffB + kSB * kBBytes;  // [epilogue warp][2] staged chu
 // weight rows of the same K step.  (Four staged output chunks per epilogue
 // warp instead of two, at the cost of one stage, made the f32 epilogues no
 // faster.)
-template <int EPI, bool WF16>
+template <int EPI, bool WF16, int BN = kBN>
 struct Plan {
   static constexpr int kStages = WF16 ? 6 : kSA;
   static constexpr int kNOut = 2;  // staged output chunks per epilogue warp
+  static constexpr int kBBytesT = (BN / 2) * kBK * 2;  // one CTA's weight rows of a K step
   static constexpr int kOffA_ = 0;
   static constexpr int kOffB_ = WF16 ? kStages * kABytes : kOffB;
-  static constexpr int kOffOut_ = WF16 ? kOffB_ + kStages * kBBytes : kOffOut;
+  static constexpr int kOffOut_ = WF16 ? kOffB_ + kStages * kBBytesT : kOffOut;
   static constexpr int kOffBar_ = kOffOut_ + 4 * kNOut * kOutBytes;
   static constexpr int kSmem_ = 1024 + kOffBar_ + 512;
   static_assert(kSmem_ <= 232448, "dynamic shared memory per block");
@@ -197,14 +198,19 @@ __device__ unsigned long long g_gemm_trace[512][8];
 #define GT_NOW() static_cast<unsigned long long>(clock64())
 #endif
 
-template <int EPI, bool WF16>
+// BN: output columns per cluster tile, 256 or (f16 weights only) 128; each
+// CTA holds BN / 2 weight rows of a tile.
+template <int EPI, bool WF16, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_q4k_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
                      const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmOut,
                      GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  using PL = Plan<EPI, WF16>;
+  static_assert(BN == 256 || (BN == 128 && WF16 && EPI != kEpiGeGLU), "128-column tiles: f16 weights only");
+  using PL = Plan<EPI, WF16, BN>;
+  constexpr int kHalfNT = BN / 2;
+  constexpr int kBBytesT = PL::kBBytesT;
   constexpr int SA = PL::kStages;  // X (and f16 B) ring depth
   uint8_t* sA = smem + PL::kOffA_;
   uint8_t* sW = smem + kOffW;
@@ -227,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ksteps = p.K / kBK;
   const int kblocks = p.K / 256;
   const int m_tiles = (p.M + kBM - 1) / kBM;
-  const int n_tiles = p.N / kBN;
+  const int n_tiles = p.N / BN;
   const int n_total = m_tiles * n_tiles;
   const int cid = static_cast<int>(cluster_id());
   const int ncl = static_cast<int>(num_clusters());
@@ -274,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = cid; tile < n_total && ok; tile += ncl) {
         const int m0 = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128;
         const int nt = tile % n_tiles;
-        const int w_row0 = EPI == kEpiGeGLU ? nt * kHalfN : nt * kBN + static_cast<int>(rank) * kHalfN;
+        const int w_row0 = EPI == kEpiGeGLU ? nt * kHalfN : nt * BN + static_cast<int>(rank) * kHalfNT;
         for (int t = 0; t < ksteps; ++t) {
           if (!WF16 && (t & 3) == 0) {
             const uint32_t sw = iw % kSW;
@@ -291,10 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef WC_GEMM_TRACE
           g_gemm_trace[blockIdx.x][4] += GT_NOW() - w0_;
 #endif
-          if (leader) mbar_arrive_expect_tx(&full_a[sa], WF16 ? 2 * (kABytes + kBBytes) : 2 * kABytes);
+          if (leader) mbar_arrive_expect_tx(&full_a[sa], WF16 ? 2 * (kABytes + kBBytesT) : 2 * kABytes);
           tma_load_2d_pair(sA + sa * kABytes, &tmA, map_to_rank(&full_a[sa], 0), t * kBK, m0);
           if (WF16)  // B stage sa holds this CTA's weight rows of the same K step
-            tma_load_2d_pair(sB + sa * kBBytes, wmap, map_to_rank(&full_a[sa], 0), t * kBK, w_row0);
+            tma_load_2d_pair(sB + sa * kBBytesT, wmap, map_to_rank(&full_a[sa], 0), t * kBK, w_row0);
           ++ia;
         }
       }
@@ -302,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN);
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
       uint32_t ia = 0, ib = 0, it = 0;
       bool ok = true;
 #ifdef WC_GEMM_TRACE
@@ -319,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         wacc_ += GT_NOW() - w0_;
 #endif
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * kBN;
+        const uint32_t d_tmem = tmem_base + buf * BN;
         for (int t = 0; t < ksteps; ++t, ++ia, ++ib) {
           const uint32_t sa = ia % SA, sb = ib % kSB;
 #ifdef WC_GEMM_TRACE
@@ -334,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
           tc_fence_after();
           const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + sa * kABytes));
-          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + (WF16 ? sa : sb) * kBBytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + (WF16 ? sa * kBBytesT : sb * kBBytes)));
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
             tc_mma_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (t > 0 || k > 0) ? 1u : 0u);
@@ -422,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
       tc_fence_after();
       const int nt = tile % n_tiles;
-      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kBN;
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       {
         // Each 128-byte-wide chunk of this warp's 32 rows is converted into
         // a swizzled staging buffer and written by one TMA tensor store
@@ -433,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // one add per element, so nothing is loaded first.
         constexpr bool kF32Out = EPI == kEpiF32 || EPI == kEpiResid;
         constexpr int kCW = kF32Out ? 32 : 64;                // output columns per chunk
-        constexpr int kOutCols = EPI == kEpiGeGLU ? kHalfN : kBN;
+        constexpr int kOutCols = EPI == kEpiGeGLU ? kHalfN : BN;
         const int col_base = nt * kOutCols;
         const int y0 = (tile / n_tiles) * kBM + static_cast<int>(rank) * 128 + q * 32;
 #pragma unroll 1
@@ -508,28 +514,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int EPI, bool WF16>
+template <int EPI, bool WF16, int BN = kBN>
 cudaError_t launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& out,
                    const GemmParams& p, int num_sms, cudaStream_t st) {
-  constexpr int smem_bytes = Plan<EPI, WF16>::kSmem_;
+  constexpr int smem_bytes = Plan<EPI, WF16, BN>::kSmem_;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm2_q4k_kernel<EPI, WF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        cudaFuncSetAttribute(gemm2_q4k_kernel<EPI, WF16, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const int tiles = ((p.M + kBM - 1) / kBM) * (p.N / kBN);
+  const int tiles = ((p.M + kBM - 1) / kBM) * (p.N / BN);
   const int clusters = std::max(1, std::min(tiles, num_sms / 2));
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  return launch_pdl(gemm2_q4k_kernel<EPI, WF16>, dim3(2 * clusters), dim3(kThreads), smem_bytes, st, attr, 1, a, w0, w1, out, p);
+  return launch_pdl(gemm2_q4k_kernel<EPI, WF16, BN>, dim3(2 * clusters), dim3(kThreads), smem_bytes, st, attr, 1, a, w0, w1, out, p);
 }
 
 }  // namespace
@@ -552,7 +558,13 @@ bool gemm2_q4k_supports(int epi, int M, int N, int K) {
 }
 
 cudaError_t gemm2_q4k_launch(int epi, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
-                             const CUtensorMap& out, const GemmParams& p, int num_sms, cudaStream_t st, bool w_f16) {
+                             const CUtensorMap& out, const GemmParams& p, int num_sms, cudaStream_t st, bool w_f16,
+                             int bn) {
+  if (bn == 128) {
+    if (!w_f16 || epi != kEpiResid || p.N % 128) return cudaErrorInvalidValue;
+    return launch<kEpiResid, true, 128>(a, w0, w1, out, p, num_sms, st);
+  }
+  if (bn != kBN) return cudaErrorInvalidValue;
   if (w_f16) {
     switch (epi) {
       case kEpiF16: return launch<kEpiF16, true>(a, w0, w1, out, p, num_sms, st);

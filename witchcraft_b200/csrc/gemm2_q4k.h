@@ -19,8 +19,11 @@ bool gemm2_q4k_supports(int epi, int M, int N, int K);
 // describe raw Q4_K rows (box kGemm2WBoxRows rows of super-blocks), or with
 // w_f16 the same weights dequantised to f16 [N][K] (box 64 x kGemm2WBoxRows,
 // 128-byte swizzle, like an activation map).
+// bn = 128 (kEpiResid on f16 weights only; weight maps with a 64-row box)
+// halves the tile width, for batches whose 256-column tiles would leave
+// clusters idle (N = 768 at a few thousand rows).
 cudaError_t gemm2_q4k_launch(int epi, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
                              const CUtensorMap& out, const GemmParams& p, int num_sms, cudaStream_t st,
-                             bool w_f16 = false);
+                             bool w_f16 = false, int bn = 256);
 
 }  // namespace wc

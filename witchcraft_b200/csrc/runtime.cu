@@ -134,6 +134,8 @@ struct LayerW {
   // The same matrices dequantised once to f16 [N][K] (the large-M GEMMs)
   __half *h_qkv, *h_o, *h_wi0, *h_wi1, *h_wo;
   CUtensorMap tmh_qkv, tmh_o, tmh_wi0, tmh_wi1, tmh_wo;
+  // O and wo f16 weights with a 64-row box, for 128-column residual tiles
+  CUtensorMap tmh64_o, tmh64_wo;
   // Raw Q4_K rows with the 2-SM kernel's box, for its fused-dequant variant
   // (handles created with WC_F16_WEIGHTS=0)
   CUtensorMap tmq2_qkv, tmq2_o, tmq2_wi0, tmq2_wi1, tmq2_wo;
@@ -320,7 +322,8 @@ int gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0,
 // runs instead; it reads the activations and the raw weights by pointer.
 int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
                const CUtensorMap& w0_2, const CUtensorMap& w1_2, int M, int N, int K, void* out, int ldo,
-               cudaStream_t st, const __half* a_ptr, const uint8_t* w0_ptr, const uint8_t* w1_ptr) {
+               cudaStream_t st, const __half* a_ptr, const uint8_t* w0_ptr, const uint8_t* w1_ptr,
+               const CUtensorMap* w_narrow = nullptr) {
   const int feat = epi == kEpiGeGLU ? N / 2 : N;
   if (gemv_q4k_supports(epi, M, feat, K)) {
     cudaError_t e = gemv_q4k_launch(epi, a_ptr, M, K, w0_ptr, w1_ptr, feat, out, ldo, h->d_status, st);
@@ -337,7 +340,13 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
     CUtensorMap tm_out;
     if (!make_out_map(&tm_out, out, M, ldo, epi == kEpiF32 || epi == kEpiResid))
       return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a GEMM output");
-    cudaError_t e = gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, device_sm_count(h->device), st, h->f16_weights);
+    // 128-column tiles for the residual GEMMs when 256-column ones would
+    // not occupy every cluster (N = 768 below about 6,300 rows)
+    const int sms = device_sm_count(h->device);
+    const bool narrow = w_narrow && h->f16_weights && epi == kEpiResid && N % 128 == 0 &&
+                        static_cast<int64_t>((M + 255) / 256) * (N / 256) < sms / 2;
+    cudaError_t e = narrow ? gemm2_q4k_launch(epi, a, *w_narrow, *w_narrow, tm_out, p, sms, st, true, 128)
+                           : gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, sms, st, h->f16_weights);
     return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
   }
   return gemm(h, epi, bn, a, w0, w1, M, N, K, out, ldo, st);
@@ -696,7 +705,8 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
            make_act_map(&w.tmh_o, w.h_o, D, I, kGemm2WBoxRows) &&
            make_act_map(&w.tmh_wi0, w.h_wi0, F, D, kGemm2WBoxRows) &&
            make_act_map(&w.tmh_wi1, w.h_wi1, F, D, kGemm2WBoxRows) &&
-           make_act_map(&w.tmh_wo, w.h_wo, D, F, kGemm2WBoxRows);
+           make_act_map(&w.tmh_wo, w.h_wo, D, F, kGemm2WBoxRows) &&
+           make_act_map(&w.tmh64_o, w.h_o, D, I, 64) && make_act_map(&w.tmh64_wo, w.h_wo, D, F, 64);
     }
     if (ok) ok = cudaStreamSynchronize(h->stream) == cudaSuccess;
     if (!ok) {
@@ -1329,13 +1339,13 @@ int forward_on(wc_t5* h, float* x, __half* xn, __half* qkv, __half* att, __half*
                                                           h->d_status, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "attention launch");
     FWD_MARK();
-    if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, h->f16_weights ? w.tmh_o : w.tmq2_o, h->f16_weights ? w.tmh_o : w.tmq2_o, M, D, I, res_out, D, st, att, w.o, w.o))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_o, tm_att, w.tm_o, w.tm_o, h->f16_weights ? w.tmh_o : w.tmq2_o, h->f16_weights ? w.tmh_o : w.tmq2_o, M, D, I, res_out, D, st, att, w.o, w.o, &w.tmh64_o))) return rc;
     FWD_MARK();
     if ((e = rmsnorm_launch(x, res_delta, w.ln1, xn, M, D, c.eps, h->d_status, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
     FWD_MARK();
     if ((rc = layer_gemm(h, kEpiGeGLU, h->bn_wi, tm_xn, w.tm_wi0, w.tm_wi1, h->f16_weights ? w.tmh_wi0 : w.tmq2_wi0, h->f16_weights ? w.tmh_wi1 : w.tmq2_wi1, M, 2 * F, D, hbuf, F, st, xn, w.wi0, w.wi1))) return rc;
     FWD_MARK();
-    if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, h->f16_weights ? w.tmh_wo : w.tmq2_wo, h->f16_weights ? w.tmh_wo : w.tmq2_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo))) return rc;
+    if ((rc = layer_gemm(h, res_epi, h->bn_wo, tm_h, w.tm_wo, w.tm_wo, h->f16_weights ? w.tmh_wo : w.tmq2_wo, h->f16_weights ? w.tmh_wo : w.tmq2_wo, M, D, F, res_out, D, st, hbuf, w.wo, w.wo, &w.tmh64_wo))) return rc;
     FWD_MARK();
     const float* next_ln = l + 1 < c.num_layers ? h->layers[l + 1].ln0 : h->final_ln;
     if ((e = rmsnorm_launch(x, res_delta, next_ln, xn, M, D, c.eps, h->d_status, st)) != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
