@@ -89,7 +89,7 @@ class ClockSampler:
                     break
                 vals = [v.strip() for v in line.strip().split(",")]
                 if len(vals) == 6:
-                    self.rows.append(vals)
+                    self.rows.append((time.time(), vals))
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
         # nvidia-smi's start-up (NVML initialisation) stalls CUDA calls of the
@@ -99,6 +99,13 @@ class ClockSampler:
         while not self.rows and time.time() - t0 < 10:
             time.sleep(0.02)
         return self
+
+    def mark(self, start: bool):
+        """Bounds of the timed region: stop() reports only samples inside it."""
+        if start:
+            self.t_start = time.time()
+        else:
+            self.t_end = time.time()
 
     def stop(self):
         self._stop.set()
@@ -110,14 +117,19 @@ class ClockSampler:
                 self._p.kill()
         if self._t:
             self._t.join(timeout=10)
-        if not self.rows:
+        t0, t1 = getattr(self, "t_start", None), getattr(self, "t_end", None)
+        rows = [v for t, v in self.rows if t0 is None or t1 is None or t0 <= t <= t1]
+        window = "timed region"
+        if not rows:  # a region shorter than the sampling period
+            rows, window = [v for _, v in self.rows], "whole sampler run (no sample inside the timed region)"
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[2 + i].lower() == "active"})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[2 + i].lower() == "active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "sm_max_mhz": float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows), "window": window}
 
 
 def _dist_env():
@@ -287,6 +299,8 @@ def run_ours(args):
     clocks = sampler()
     barrier()
     torch.cuda.synchronize()
+    if clocks:
+        clocks.mark(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for s in range(args.warmup, args.warmup + args.steps):
@@ -294,6 +308,8 @@ def run_ours(args):
     e1.record(stream)
     enc.sync(stream.cuda_stream)
     torch.cuda.synchronize()
+    if clocks:
+        clocks.mark(False)
     barrier()
     clk = clocks.stop() if clocks else None
     ms = e0.elapsed_time(e1)
@@ -336,12 +352,16 @@ def run_ours(args):
     e2e_step([biggest, biggest])
     clocks = sampler()
     barrier()
+    if clocks:
+        clocks.mark(True)
     t0 = time.perf_counter()
     t_steps = []
     for s0 in range(0, len(timed), per_step):
         e2e_step(timed[s0:s0 + per_step])
         t_steps.append(time.perf_counter())
     t_local = time.perf_counter() - t0
+    if clocks:
+        clocks.mark(False)
     barrier()
     clk_e2e = clocks.stop() if clocks else None
     t_e2e = max_over_ranks(t_local)
