@@ -49,7 +49,7 @@ LAUNCHES_PER_FORWARD_PER_LAYER = 7   # qkv gemm, attention, o gemm, rmsnorm, wi 
 # dram read+write bytes per launch of the dominant kernel (the gated-GELU GEMM
 # at M = 16,384), from one ncu capture of `bench.py --profile-kernel geglu`
 # (dram__bytes_read.sum + dram__bytes_write.sum); re-captured when the kernel changes
-NCU_TRAFFIC_BYTES = 49226240  # 31.49 MB read + 17.74 MB written
+NCU_TRAFFIC_BYTES = 49352960  # 31.49 MB read + 17.86 MB written
 
 
 def _peaks():
