@@ -10,7 +10,8 @@ import os
 import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libwc_t5cuda.so")
+# WC_T5CUDA_LIB names another build of the same library (A/B measurements)
+LIB_PATH = os.environ.get("WC_T5CUDA_LIB") or os.path.join(HERE, "libwc_t5cuda.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 HEADER = os.path.join(INCLUDE, "wc_t5cuda.h")
 
