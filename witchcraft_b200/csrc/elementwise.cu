@@ -114,6 +114,54 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
   report_f16_clip(clip, status);
 }
 
+// The same normalisation for D = 768 without a residual add (the large-M
+// forward, whose GEMMs already added it): each warp normalises two rows and
+// issues all twelve 16-byte loads of a lane before any arithmetic, so their
+// latencies overlap.  Per row the arithmetic is rownorm_row's, in the same
+// order, so the results are the same bits.
+__global__ void rmsnorm768x2_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                    __half* __restrict__ y, int M, float eps, uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_launch_next();
+  constexpr int D = 768, G = D / 128;
+  const int m0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2;
+  const int lane = threadIdx.x & 31;
+  if (m0 >= M) return;
+  const bool two = m0 + 1 < M;
+  float4 v[2][G];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(two ? m0 + r : m0) * D);
+#pragma unroll
+    for (int g = 0; g < G; ++g) v[r][g] = xr[lane + 32 * g];
+  }
+  float ss[2] = {0.f, 0.f};
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      ss[r] += v[r][g].x * v[r][g].x + v[r][g].y * v[r][g].y + v[r][g].z * v[r][g].z + v[r][g].w * v[r][g].w;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) ss[r] = rownorm_warp_sum(ss[r]);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  bool clip = false;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (r == 1 && !two) break;
+    const float inv = 1.0f / sqrtf(ss[r] / static_cast<float>(D) + eps);
+    uint2* yr = reinterpret_cast<uint2*>(y + static_cast<size_t>(m0 + r) * D);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4 ww = wr[lane + 32 * g];
+      uint2 o;
+      o.x = pack_f16x2_sat(v[r][g].x * inv * ww.x, v[r][g].y * inv * ww.y, clip);
+      o.y = pack_f16x2_sat(v[r][g].z * inv * ww.z, v[r][g].w * inv * ww.w, clip);
+      yr[lane + 32 * g] = o;
+    }
+  }
+  report_f16_clip(clip, status);
+}
+
 // A wait on an mbarrier that nothing ever arrives on, bounded by limit_ns:
 // exercises the timeout path every pipelined kernel uses.
 __global__ void wait_timeout_selftest_kernel(uint32_t* status, uint64_t limit_ns) {
@@ -162,6 +210,9 @@ cudaError_t rmsnorm_launch(float* x, const float* delta, const float* w, __half*
                            uint32_t* status, cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (D % 128 != 0 || D > kMaxD) return cudaErrorInvalidValue;
+  if (D == 768 && delta == nullptr)
+    return launch_pdl(rmsnorm768x2_kernel, dim3((M + 15) / 16), dim3(256), 0, st, nullptr, 0,
+                      static_cast<const float*>(x), w, y, M, eps, status);
   return launch_pdl(rmsnorm_kernel, dim3((M + 7) / 8), dim3(256), 0, st, nullptr, 0, x, delta, w, y, M, D, eps, status);
 }
 
