@@ -37,6 +37,7 @@
 #include "q4k.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace wc {
 
@@ -192,7 +193,7 @@ __device__ __forceinline__ uint4 dequant8_f16(uint32_t x0, uint32_t x1, uint64_t
 // Optional wait accounting for pipeline analysis (off in the library build):
 // per CTA, cycles the MMA thread waited for accumulators / operand stages and
 // its loop total, the producer's waits for free stages, the first epilogue
-// warp's waits for accumulators.
+// warp's waits for accumulators, and the global timer at entry and exit.
 #ifdef WC_GEMM_TRACE
 __device__ unsigned long long g_gemm_trace[512][8];
 #define GT_NOW() static_cast<unsigned long long>(clock64())
@@ -228,6 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+#ifdef WC_GEMM_TRACE
+  if (threadIdx.x == 0) g_gemm_trace[blockIdx.x][5] = global_timer_ns();
+#endif
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const int ksteps = p.K / kBK;
@@ -508,6 +512,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   cluster_sync();
+#ifdef WC_GEMM_TRACE
+  if (threadIdx.x == 0) g_gemm_trace[blockIdx.x][7] = global_timer_ns();
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
@@ -552,6 +559,19 @@ extern "C" int wc_gemm_trace(unsigned long long* host, int reset) {
 }
 #endif
 
+int gemm2_resid_bn(int M, int N, int num_sms) {
+  // WC_RESID_BN=128 / 256 forces the width (A/B runs)
+  static const int forced = [] {
+    const char* e = std::getenv("WC_RESID_BN");
+    return e ? std::atoi(e) : 0;
+  }();
+  if ((forced == 128 && N % 128 == 0) || (forced == 256 && N % kBN == 0)) return forced;
+  if (N % kBN != 0) return 128;
+  const int64_t clusters = std::max(1, num_sms / 2);
+  const int64_t t128 = static_cast<int64_t>((M + kBM - 1) / kBM) * (N / 128);
+  return t128 <= clusters ? 128 : kBN;
+}
+
 bool gemm2_q4k_supports(int epi, int M, int N, int K) {
   return (epi == kEpiF16 || epi == kEpiGeGLU || epi == kEpiResid || epi == kEpiF32) && M >= 1 && N % kBN == 0 &&
          K % 256 == 0 && K >= 256;
@@ -561,8 +581,10 @@ cudaError_t gemm2_q4k_launch(int epi, const CUtensorMap& a, const CUtensorMap& w
                              const CUtensorMap& out, const GemmParams& p, int num_sms, cudaStream_t st, bool w_f16,
                              int bn) {
   if (bn == 128) {
-    if (!w_f16 || epi != kEpiResid || p.N % 128) return cudaErrorInvalidValue;
-    return launch<kEpiResid, true, 128>(a, w0, w1, out, p, num_sms, st);
+    if (!w_f16 || p.N % 128) return cudaErrorInvalidValue;
+    if (epi == kEpiResid) return launch<kEpiResid, true, 128>(a, w0, w1, out, p, num_sms, st);
+    if (epi == kEpiF32) return launch<kEpiF32, true, 128>(a, w0, w1, out, p, num_sms, st);
+    return cudaErrorInvalidValue;
   }
   if (bn != kBN) return cudaErrorInvalidValue;
   if (w_f16) {

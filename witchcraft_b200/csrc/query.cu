@@ -132,12 +132,14 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
   }
   float smax = active ? missing[lane] : 0.0f;
   const float* cs_t = cscores + static_cast<int64_t>(active ? lane : 0) * n_cent;
-  // The codes of the next R rows are fetched (into registers) while the
-  // current R rows are scored, so their global-memory latency overlaps the
-  // fmaf chains.  Raw (unindexed) rows are read when their turn comes.
+  // The codes and centroid scores of the next R rows are fetched (into
+  // registers) while the current R rows are scored, so their global-memory
+  // latency overlaps the fmaf chains.  Raw (unindexed) rows are read when
+  // their turn comes.
   const int64_t g0 = doc_start[d], g1 = doc_start[d + 1];
   int64_t g = g0, p = g0 < g1 ? group_start[g0] : 0;
-  auto next_rows = [&](int64_t& gg, int64_t& pp, int64_t (&rid)[R], uchar2 (&cb)[R], int& nr, int64_t& grp) {
+  auto next_rows = [&](int64_t& gg, int64_t& pp, int64_t (&rid)[R], uchar2 (&cb)[R], float (&cv)[R], int& nr,
+                       int64_t& grp) {
     // the rows [pp, pp + nr) of group gg (nr = 0 past the document)
     while (gg < g1 && pp >= group_start[gg + 1]) {
       ++gg;
@@ -154,6 +156,9 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
       cb[rr] = (rr < nr && rid[rr] < n_idx) ? *reinterpret_cast<const uchar2*>(codes + rid[rr] * (D / 2) + 2 * lane)
                                             : make_uchar2(0, 0);
     }
+    // the centroid score of each indexed row for this lane's token
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) cv[rr] = (rr < nr && rid[rr] < n_idx) ? cs_t[cluster[rid[rr]]] : 0.0f;
     pp += nr;
   };
   // score of groups [ga, gb) given the running maxima (one sum, written to
@@ -172,8 +177,9 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
   };
   int64_t rid[R], grp;
   uchar2 cb[R];
+  float cv[R];
   int nr;
-  next_rows(g, p, rid, cb, nr, grp);
+  next_rows(g, p, rid, cb, cv, nr, grp);
   emit(g0, nr > 0 ? grp : g1);  // leading groups without rows
   while (nr > 0) {
     __syncwarp();
@@ -192,9 +198,13 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
     const int cur_nr = nr;
     const int64_t cur_grp = grp;
     int64_t cur_rid[R];
+    float cur_cv[R];
 #pragma unroll
-    for (int rr = 0; rr < R; ++rr) cur_rid[rr] = rid[rr];
-    next_rows(g, p, rid, cb, nr, grp);  // prefetch
+    for (int rr = 0; rr < R; ++rr) {
+      cur_rid[rr] = rid[rr];
+      cur_cv[rr] = cv[rr];
+    }
+    next_rows(g, p, rid, cb, cv, nr, grp);  // prefetch
     float acc[R];
 #pragma unroll
     for (int rr = 0; rr < R; ++rr) acc[rr] = 0.0f;
@@ -213,7 +223,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
     for (int rr = 0; rr < R; ++rr) {
       if (rr < cur_nr && active) {
         float a = acc[rr];
-        if (cur_rid[rr] < n_idx) a = __fadd_rn(a, cs_t[cluster[cur_rid[rr]]]);
+        if (cur_rid[rr] < n_idx) a = __fadd_rn(a, cur_cv[rr]);
         smax = fmaxf(smax, a);
       }
     }

@@ -340,11 +340,10 @@ int layer_gemm(wc_t5* h, int epi, int bn, const CUtensorMap& a, const CUtensorMa
     CUtensorMap tm_out;
     if (!make_out_map(&tm_out, out, M, ldo, epi == kEpiF32 || epi == kEpiResid))
       return fail(h, WC_E_CUDA, "cuTensorMapEncodeTiled failed for a GEMM output");
-    // 128-column tiles for the residual GEMMs when 256-column ones would
-    // not occupy every cluster (N = 768 below about 6,300 rows)
+    // 128-column tiles for the residual GEMMs when their cluster rounds are
+    // shorter in total than with 256-column tiles
     const int sms = device_sm_count(h->device);
-    const bool narrow = w_narrow && h->f16_weights && epi == kEpiResid && N % 128 == 0 &&
-                        static_cast<int64_t>((M + 255) / 256) * (N / 256) < sms / 2;
+    const bool narrow = w_narrow && h->f16_weights && epi == kEpiResid && gemm2_resid_bn(M, N, sms) == 128;
     cudaError_t e = narrow ? gemm2_q4k_launch(epi, a, *w_narrow, *w_narrow, tm_out, p, sms, st, true, 128)
                            : gemm2_q4k_launch(epi, a, w0_2, w1_2, tm_out, p, sms, st, h->f16_weights);
     return e == cudaSuccess ? WC_OK : cuda_fail(h, e, "GEMM launch");
@@ -1099,9 +1098,14 @@ extern "C" int wc_gemm_f16(const void* d_x, int M, int K, const void* d_w, const
   if (epilogue == kEpiGeGLU && !d_w_up) return WC_E_INVALID_ARG;
   const int tile_n = epilogue == kEpiGeGLU ? 2 * N : N;
   if (!gemm2_q4k_supports(epilogue, M, tile_n, K)) return WC_E_UNSUPPORTED;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = device_sm_count(dev);
+  // the f32 epilogues take the tile width the encoder picks for its residual GEMMs
+  const int bn = (epilogue == kEpiResid || epilogue == kEpiF32) ? gemm2_resid_bn(M, N, sms) : 256;
   CUtensorMap ta, tw0, tw1, tout;
-  if (!make_act_map(&ta, d_x, M, K) || !make_act_map(&tw0, d_w, N, K, kGemm2WBoxRows) ||
-      !make_act_map(&tw1, epilogue == kEpiGeGLU ? d_w_up : d_w, N, K, kGemm2WBoxRows) ||
+  if (!make_act_map(&ta, d_x, M, K) || !make_act_map(&tw0, d_w, N, K, bn / 2) ||
+      !make_act_map(&tw1, epilogue == kEpiGeGLU ? d_w_up : d_w, N, K, bn / 2) ||
       !make_out_map(&tout, d_out, M, N, epilogue == kEpiF32 || epilogue == kEpiResid))
     return WC_E_CUDA;
   GemmParams p{};
@@ -1112,10 +1116,8 @@ extern "C" int wc_gemm_f16(const void* d_x, int M, int K, const void* d_w, const
   p.ldo = N;
   p.status = kernel_status_word();
   if (!p.status) return WC_E_CUDA;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  return gemm2_q4k_launch(epilogue, ta, tw0, tw1, tout, p, device_sm_count(dev), static_cast<cudaStream_t>(stream),
-                          true) == cudaSuccess
+  return gemm2_q4k_launch(epilogue, ta, tw0, tw1, tout, p, sms, static_cast<cudaStream_t>(stream), true, bn) ==
+                 cudaSuccess
              ? WC_OK
              : WC_E_CUDA;
 }
