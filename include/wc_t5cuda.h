@@ -191,7 +191,8 @@ int wc_gemm_f16(const void* d_x, int M, int K, const void* d_w_f16, const void* 
 
 /* Encoder self-attention (src/quantized_t5.rs:426-500) over a padded batch.
  * d_qkv f16 [B*L][3*H*64] (q | k | v), d_out f16 [B*L][H*64], d_lengths
- * i32 [B], d_bias_table f32 [num_buckets][H] (relative_attention_bias).
+ * i32 [B], d_bias_table f32 [num_buckets][H] (relative_attention_bias),
+ * 2 <= num_buckets <= 32 (T5 uses 32).
  * No 1/sqrt(d) scaling; keys >= lengths[b] are masked. */
 int wc_attention(const void* d_qkv, int B, int L, int H, const int32_t* d_lengths, const float* d_bias_table,
                  int num_buckets, int max_distance, void* d_out, void* stream);

@@ -74,10 +74,14 @@ constexpr int kQBytes = kQ * 128;      // 128 x 64 f16
 constexpr int kKVBytes = kKeys * 128;  // 64 x 64 f16
 constexpr int kWin = kQ + kKeys - 1;   // distinct key - query offsets of one tile pair
 constexpr int kMaxHeads = 32;          // bias tables of all heads stay in shared memory
-constexpr int kKVStages = 2;
+// K runs three stages deep, so the load of K(t) can start once S(t - 3) is
+// done, a whole softmax step before S(t - 2) would free a two-stage ring; V
+// keeps two stages (it is needed a step after K)
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr int kOffQ = 0;                              // 2 buffers
-constexpr int kOffK = kOffQ + 2 * kQBytes;            // kKVStages stages
-constexpr int kOffV = kOffK + kKVStages * kKVBytes;   // kKVStages stages
+constexpr int kOffK = kOffQ + 2 * kQBytes;            // kKStages stages
+constexpr int kOffV = kOffK + kKStages * kKVBytes;    // kVStages stages
 constexpr int kMaxL = 2048;
 // Bias row of one item: bias[x] for key - query = x - q0 - (kQ - 1), built
 // once per item, in two copies, the second shifted by one entry, so that
@@ -86,10 +90,11 @@ constexpr int kMaxL = 2048;
 // same offsets from different copies fall in different banks.
 constexpr int kBiasPad = 2256;
 static_assert(kBiasPad >= kMaxL + kWin + 1 && kBiasPad % 32 == 16, "bias row copies");
-constexpr int kOffBias = kOffV + kKVStages * kKVBytes;  // f32 [2 copies][kBiasPad]
-constexpr int kOffTab = kOffBias + 2 * kBiasPad * 4;   // f32 [kMaxHeads][64]
-constexpr int kOffThr = kOffTab + kMaxHeads * 64 * 4;  // int [32]
-constexpr int kMaxSortSeqs = 2048;  // larger batches keep their own sequence order
+constexpr int kOffBias = kOffV + kVStages * kKVBytes;  // f32 [2 copies][kBiasPad]
+constexpr int kMaxBuckets = 32;                        // T5's relative_attention_num_buckets
+constexpr int kOffTab = kOffBias + 2 * kBiasPad * 4;   // f32 [kMaxHeads][kMaxBuckets]
+constexpr int kOffThr = kOffTab + kMaxHeads * kMaxBuckets * 4;  // int [32]
+constexpr int kMaxSortSeqs = 1024;  // larger batches keep their own sequence order
 constexpr int kOffOrder = kOffThr + 32 * 4;            // u32 [kMaxSortSeqs]: b | length << 16
 constexpr int kOffHist = kOffOrder + kMaxSortSeqs * 4;                   // int [64]
 // bucket of every key - query offset an item's bias row can need: index
@@ -217,11 +222,13 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars;                        // [2] per Q buffer
   uint64_t* q_empty = bars + 2;                   // [2] the item's last S is done
-  // K / V stage t % 2 is free again once S(t) / P(t) V(t) is done, which
-  // s_full / o_done of that step report (no separate empty barriers)
-  uint64_t* k_full = bars + 4;                    // [kKVStages]
-  uint64_t* v_full = k_full + kKVStages;          // [kKVStages]
-  uint64_t* s_full = v_full + kKVStages;          // [2] per S buffer
+  // K stage t % 3 is free again once S(t) is done (k_empty, committed with
+  // it); V stage t % 2 once P(t) V(t) is done, which o_done of that step
+  // reports
+  uint64_t* k_full = bars + 4;                    // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;          // [kKStages]
+  uint64_t* v_full = k_empty + kKStages;          // [kVStages]
+  uint64_t* s_full = v_full + kVStages;           // [2] per S buffer
   // [2] by step parity (4 softmax warps arrive): the warps do not step in
   // lockstep, one may arrive for step t + 1 before another for step t, but
   // never for t + 2 (S(t + 2) is issued only after P(t))
@@ -246,10 +253,11 @@ __global__ void __launch_bounds__(kThreads)
   const int inner = H * kDh;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kKVStages; ++i) {
+    for (int i = 0; i < kKStages; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
+      mbar_init(&k_empty[i], 1);
     }
+    for (int i = 0; i < kVStages; ++i) mbar_init(&v_full[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
@@ -268,7 +276,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x < 32) sThr[threadIdx.x] = bt.thr[threadIdx.x];
   for (int i = threadIdx.x; i < H * 2 * bt.half; i += blockDim.x) {
     const int h = i / (2 * bt.half), bk = i % (2 * bt.half);
-    sTab[h * 64 + bk] = bias_tab[bk * H + h] * 1.4426950408889634f;
+    sTab[h * kMaxBuckets + bk] = bias_tab[bk * H + h] * 1.4426950408889634f;
   }
   tc_fence_before();
   __syncthreads();
@@ -280,7 +288,9 @@ __global__ void __launch_bounds__(kThreads)
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       // Q of the g-th active item into buffer g % 2 (free once the last S
-      // of item g - 2 is done)
+      // of item g - 2 is done), one item ahead.  Issuing it later (after the
+      // step's K and V loads, or only once its buffer is free) measured
+      // slower: the next item's first S then waits for Q.
       auto load_q = [&](const Item& it, int g) -> bool {
         if (!mbar_wait(&q_empty[g & 1], ((g >> 1) & 1) ^ 1, status)) return false;
         ATRACE(22);
@@ -291,31 +301,44 @@ __global__ void __launch_bounds__(kThreads)
         tma_load_2d(dst + kQBytes / 2, &tmQKV, &q_full[g & 1], it.h * kDh, row + 64);
         return true;
       };
+      // V(t) waits for P(t - 2) V(t - 2), which comes a softmax step after
+      // S(t - 2); loading it one iteration late, after K(t + 1), keeps that
+      // wait from holding back the next K load.
+      auto load_v = [&](int tv, int col, int row) -> bool {
+        // V stage tv % 2 last held V(tv - 2), free once P(tv - 2) V(tv - 2) is
+        // done: o_done of that step (2 stages, 2 barriers: same index and parity)
+        static_assert(kVStages == 2, "V stages are freed through the per-step P V barriers");
+        const int s = tv % kVStages;
+        if (!mbar_wait(&o_done[s], ((tv / kVStages) & 1) ^ 1, status)) return false;
+        ATRACE(21);
+        mbar_arrive_expect_tx(&v_full[s], kKVBytes);
+        tma_load_2d(sV + s * kKVBytes, &tmQKV, &v_full[s], col, row);
+        return true;
+      };
       Cursor c = start;
       bool ok = !c.valid(il) || load_q(c.it, 0);
-      for (int t = 0; c.valid(il) && ok; ++t) {
+      int v_col = 0, v_row = 0;  // V tile of the previous step
+      int t = 0;
+      for (; c.valid(il) && ok; ++t) {
         if (c.j == 0) {
           // one item ahead
           const Item nx = il.next_active(c.it.round + 1);
           if (nx.id < il.n_items && !(ok = load_q(nx, c.g + 1))) break;
         }
-        const int s = t % kKVStages;
-        const uint32_t par = ((t / kKVStages) & 1) ^ 1;
+        const int s = t % kKStages;
         const int krow = c.it.b * L + c.j * kKeys;
-        // stage s last held K(t - 2), free once S(t - 2) is done: s_full of
-        // that step (2 stages and 2 S buffers, so the same index and parity)
-        static_assert(kKVStages == 2, "K / V stages are freed through the per-step S / P V barriers");
-        if (!(ok = mbar_wait(&s_full[s], par, status))) break;
+        // stage s last held K(t - 3), free once S(t - 3) is done
+        if (!(ok = mbar_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1, status))) break;
         ATRACE(20);
         mbar_arrive_expect_tx(&k_full[s], kKVBytes);
         tma_load_2d(sK + s * kKVBytes, &tmQKV, &k_full[s], inner + c.it.h * kDh, krow);
-        // and V(t - 2), free once P(t - 2) V(t - 2) is done
-        if (!(ok = mbar_wait(&o_done[s], par, status))) break;
-        ATRACE(21);
-        mbar_arrive_expect_tx(&v_full[s], kKVBytes);
-        tma_load_2d(sV + s * kKVBytes, &tmQKV, &v_full[s], 2 * inner + c.it.h * kDh, krow);
+        // V(t - 1) into its stage, free once P(t - 3) V(t - 3) is done
+        if (t > 0 && !(ok = load_v(t - 1, v_col, v_row))) break;
+        v_col = 2 * inner + c.it.h * kDh;
+        v_row = krow;
         c.advance(il);
       }
+      if (ok && t > 0) load_v(t - 1, v_col, v_row);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -325,12 +348,19 @@ __global__ void __launch_bounds__(kThreads)
       bool ok = true;
       Cursor cs = start;  // next S to issue (two steps ahead of P V)
       int ts = 0;
-      // S(ts) = Q K_j^T into S buffer ts % 2 (needs its Q and K stage)
-      auto issue_s = [&]() -> bool {
-        const int s = ts % kKVStages;
+      // Inputs of S(ts): its Q (first key tile of an item) and K stage.
+      // Waited for before the P of the step that issues it, so that only
+      // the MMAs and commits follow the softmax warps' signal.
+      auto wait_s_inputs = [&]() -> bool {
+        const int s = ts % kKStages;
         if (cs.j == 0 && !mbar_wait(&q_full[cs.g & 1], (cs.g >> 1) & 1, status)) return false;
-        if (!mbar_wait(&k_full[s], (ts / kKVStages) & 1, status)) return false;
+        if (!mbar_wait(&k_full[s], (ts / kKStages) & 1, status)) return false;
         ATRACE(15);
+        return true;
+      };
+      // S(ts) = Q K_j^T into S buffer ts % 2
+      auto issue_s = [&]() {
+        const int s = ts % kKStages;
         tc_fence_after();
         const uint64_t qa = sw128_kmajor_desc(smem_u32(sQ + (cs.g & 1) * kQBytes));
         const uint64_t bk = sw128_kmajor_desc(smem_u32(sK + s * kKVBytes));
@@ -339,21 +369,28 @@ __global__ void __launch_bounds__(kThreads)
           tc_mma_f16(tmem + kColS + 64 * (ts & 1), qa + 2 * k, bk + 2 * k, idesc_qk, k > 0);
         ATRACE(16);
         tc_commit(&s_full[ts & 1]);
+        tc_commit(&k_empty[s]);
         ATRACE(12);
         if (cs.j == cs.it.n_kt - 1) tc_commit(&q_empty[cs.g & 1]);
+      };
+      for (int k = 0; k < 2 && cs.valid(il) && ok; ++k) {
+        if (!(ok = wait_s_inputs())) break;
+        issue_s();
         cs.advance(il);
         ++ts;
-        return true;
-      };
-      for (int k = 0; k < 2 && cs.valid(il) && ok; ++k) ok = issue_s();
+      }
       Cursor cp = start;
       for (int t = 0; cp.valid(il) && ok; ++t) {
-        const int s = t % kKVStages;
+        const int s = t % kVStages;
+        // S(t + 2) goes into S buffer t % 2 right after P(t) V(t) in issue
+        // order (the tensor pipe runs them in order, so P(t) is read first)
+        const bool has_s = cs.valid(il);
+        if (has_s && !(ok = wait_s_inputs())) break;
+        if (!(ok = mbar_wait(&v_full[s], (t / kVStages) & 1, status))) break;
+        ATRACE(13);
         // P(t) of item g also means the epilogue of item g - 2 has read O buffer g % 2
         if (!(ok = mbar_wait(&p_full[t & 1], (t >> 1) & 1, status))) break;
         ATRACE(10);
-        if (!(ok = mbar_wait(&v_full[s], (t / kKVStages) & 1, status))) break;
-        ATRACE(13);
         tc_fence_after();
         const uint64_t v = sw128_mnmajor_desc(smem_u32(sV + s * kKVBytes));
         const uint32_t pa = tmem + kColS + 64 * (t & 1);
@@ -364,8 +401,12 @@ __global__ void __launch_bounds__(kThreads)
         ATRACE(14);
         tc_commit(&o_done[t & 1]);
         ATRACE(11);
+        if (has_s) issue_s();
         cp.advance(il);
-        if (cs.valid(il)) ok = issue_s();  // S buffer t % 2 is free again
+        if (has_s) {
+          cs.advance(il);
+          ++ts;
+        }
       }
     }
   } else {
@@ -449,7 +490,7 @@ __global__ void __launch_bounds__(kThreads)
       if (lane == 0) ATRACE(2);
       asm volatile("bar.sync 1, 128;" ::: "memory");
       {
-        const float* tab = sTab + it.h * 64;
+        const float* tab = sTab + it.h * kMaxBuckets;
         const uint8_t* bk = sBkt + kBktHalf - it.q0 - (kQ - 1);
         for (int x = st; x < it.n_kt * kKeys + kWin; x += 128) {
           const float w = tab[bk[x]];
@@ -535,6 +576,7 @@ __global__ void __launch_bounds__(kThreads)
             }
           }
         }
+        tmem_wait_st();  // P (and a rescaled O) complete before the MMA thread is told
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t & 1]);
@@ -585,7 +627,7 @@ cudaError_t attention_tc_launch(const CUtensorMap& tm_qkv, __half* out, const in
                                 const float* bias_tab, const BucketThresholds& bt, uint32_t* status,
                                 cudaStream_t st) {
   if (B <= 0 || L <= 0) return cudaSuccess;
-  if (L > kMaxL || 2 * bt.half > 64 || H <= 0 || H > kMaxHeads) return cudaErrorInvalidValue;
+  if (L > kMaxL || 2 * bt.half > kMaxBuckets || H <= 0 || H > kMaxHeads) return cudaErrorInvalidValue;
   const int64_t n_items = static_cast<int64_t>((L + kQ - 1) / kQ) * B * H;
   if (n_items > INT32_MAX || static_cast<int64_t>(B) * L > INT32_MAX) return cudaErrorInvalidValue;
   static bool attr_set[64] = {};

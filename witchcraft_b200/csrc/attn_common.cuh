@@ -44,6 +44,9 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32_nowait(uint32_t taddr, float*
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Completes this thread's earlier tcgen05.st, so that an MMA issued by another
+// thread after the next thread synchronisation reads the stored columns.
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ float ex2(float x) {
   float y;

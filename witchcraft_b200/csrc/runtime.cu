@@ -485,7 +485,7 @@ extern "C" int wc_t5_create(int device_ordinal, const uint8_t* gguf, size_t gguf
     return fail(nullptr, WC_E_UNSUPPORTED, "only the gated-gelu feed-forward (XTR / T5 v1.1) is supported");
   if (cfg.d_kv != 64) return fail(nullptr, WC_E_UNSUPPORTED, "d_kv must be 64");
   if (cfg.d_model % 256 || cfg.d_model > 1024 || cfg.d_ff % 256 || (cfg.num_heads * 64) % 256 ||
-      cfg.num_layers < 1 || cfg.num_buckets < 2 || cfg.num_buckets > 64 || cfg.vocab_size < 1)
+      cfg.num_layers < 1 || cfg.num_buckets < 2 || cfg.num_buckets > 32 || cfg.vocab_size < 1)
     return fail(nullptr, WC_E_UNSUPPORTED, "unsupported model dimensions in config.json");
   std::unordered_map<std::string, GgufTensor> t;
   if (!gguf_parse(gguf, gguf_len, &t, &err)) return fail(nullptr, WC_E_GGUF, err);
@@ -1199,7 +1199,7 @@ extern "C" int wc_attention(const void* d_qkv, int B, int L, int H, const int32_
                             const float* d_bias_table, int num_buckets, int max_distance, void* d_out,
                             void* stream) {
   if (!d_qkv || !d_lengths || !d_bias_table || !d_out || B < 1 || L < 1 || L > kMaxL || H < 1 ||
-      num_buckets < 2 || num_buckets > 64 || max_distance < 1)
+      num_buckets < 2 || num_buckets > 32 || max_distance < 1)
     return WC_E_INVALID_ARG;
   const BucketThresholds bt = cached_thresholds(num_buckets, max_distance);
   if (attention_small_supports(L))
