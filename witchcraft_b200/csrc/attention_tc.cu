@@ -240,8 +240,6 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* o_done = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
-  pdl_wait();  // before lengths and any activation (see pdl_wait)
-  pdl_launch_next();  // after the wait: at most one grid waits ahead
 #ifdef WC_ATTN_TRACE
   int tr_n = 0;
 #endif
@@ -278,10 +276,23 @@ __global__ void __launch_bounds__(kThreads)
     const int h = i / (2 * bt.half), bk = i % (2 * bt.half);
     sTab[h * kMaxBuckets + bk] = bias_tab[bk * H + h] * 1.4426950408889634f;
   }
+  // buckets of the offsets this launch can meet (|delta| < L + kWin), from
+  // the thresholds once they are in shared memory
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * (L + kWin) - 1; i += kThreads) {
+    const int delta = i - (L + kWin - 1);
+    sBkt[delta + kBktHalf] = static_cast<uint8_t>(rel_bucket_tc(sThr, bt.half, delta));
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Everything above reads no activation: the relative-bias weights, the
+  // launch's bucket thresholds, and the lengths, which every forward copies
+  // in before its first kernel.  So it runs before the wait for the previous
+  // kernel (the QKV GEMM) and overlaps that kernel's last round.
+  pdl_wait();
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
   const Cursor start{il.next_active(0), 0, 0};
 
   if (warp == 0) {
@@ -413,12 +424,6 @@ __global__ void __launch_bounds__(kThreads)
     // ------------------------------------------------------------ softmax + epilogue
     const int st = threadIdx.x - 64;  // 0..127
     const int qd = warp & 3;          // TMEM lane quarter
-    // buckets of the offsets this launch can meet (|delta| < L + kWin); the
-    // first item's barrier below orders these writes before their use
-    for (int i = st; i < 2 * (L + kWin) - 1; i += 128) {
-      const int delta = i - (L + kWin - 1);
-      sBkt[delta + kBktHalf] = static_cast<uint8_t>(rel_bucket_tc(sThr, bt.half, delta));
-    }
     const int r = qd * 32 + lane;     // query row within the tile
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     // Epilogue of an item whose O is final once P V of its last step t_last
