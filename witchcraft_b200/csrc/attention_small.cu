@@ -30,9 +30,8 @@ __global__ void __launch_bounds__(KL * 2)
                            const int32_t* __restrict__ lengths, int L, int H, const float* __restrict__ bias_tab,
                            BucketThresholds bt) {
   __shared__ __align__(16) uint8_t smem[attn_small::smem_bytes(KL)];
-  pdl_wait();
-  pdl_launch_next();
-  attn_small::item<KL>(qkv, out, lengths, L, H, bias_tab, bt, blockIdx.y, blockIdx.x, smem);
+  // the item waits for the previous kernel once its bias row is built
+  attn_small::item<KL>(qkv, out, lengths, L, H, bias_tab, bt, blockIdx.y, blockIdx.x, smem, true);
 }
 
 }  // namespace

@@ -60,7 +60,7 @@ template <int KL>
 __device__ __forceinline__ void item(const __half* __restrict__ qkv, __half* __restrict__ out,
                                      const int32_t* __restrict__ lengths, int L, int H,
                                      const float* __restrict__ bias_tab, const BucketThresholds& bt, int b, int h,
-                                     uint8_t* smem) {
+                                     uint8_t* smem, bool pdl) {
   uint8_t* sQ = smem;
   uint8_t* sK = smem + KL * kRowB;
   uint8_t* sV = smem + 2 * KL * kRowB;
@@ -70,6 +70,15 @@ __device__ __forceinline__ void item(const __half* __restrict__ qkv, __half* __r
   const int len = min(max(lengths[b], 0), L);
   const int inner = H * kDh;
   const size_t row0 = static_cast<size_t>(b) * L;
+  // the bias row reads only weights and the launch's thresholds: with pdl it
+  // is built before the wait for the previous kernel (which writes qkv)
+  if (tid < 2 * bt.half) sCol[tid] = bias_tab[tid * H + h] * 1.4426950408889634f;
+  __syncthreads();
+  for (int i = tid; i < 2 * KL - 1; i += kT) sBias[i] = sCol[bucket_of(bt, i - (KL - 1))];
+  if (pdl) {
+    pdl_wait();
+    pdl_launch_next();  // after the wait: at most one grid waits ahead
+  }
   if (len == 0) {
     for (int i = tid; i < L * (kDh / 8); i += kT) {
       const int r = i >> 3, c = i & 7;
@@ -84,9 +93,6 @@ __device__ __forceinline__ void item(const __half* __restrict__ qkv, __half* __r
     cp16s(dst, qkv + (row0 + (r < L ? r : 0)) * (3 * inner) + mat * inner + h * kDh + c * 8, r < L);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
-  if (tid < 2 * bt.half) sCol[tid] = bias_tab[tid * H + h] * 1.4426950408889634f;
-  __syncthreads();
-  for (int i = tid; i < 2 * KL - 1; i += kT) sBias[i] = sCol[bucket_of(bt, i - (KL - 1))];
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   const int q0 = warp * 16;

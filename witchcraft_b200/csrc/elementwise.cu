@@ -121,11 +121,17 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
 // order, so the results are the same bits.
 __global__ void rmsnorm768x2_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                     __half* __restrict__ y, int M, float eps, uint32_t* __restrict__ status) {
-  pdl_wait();
-  pdl_launch_next();
   constexpr int D = 768, G = D / 128;
   const int m0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2;
   const int lane = threadIdx.x & 31;
+  // the norm weights are not written by the previous kernel: load them
+  // before waiting for it
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4 ww[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) ww[g] = wr[lane + 32 * g];
+  pdl_wait();
+  pdl_launch_next();
   if (m0 >= M) return;
   const bool two = m0 + 1 < M;
   float4 v[2][G];
@@ -143,7 +149,6 @@ __global__ void rmsnorm768x2_kernel(const float* __restrict__ x, const float* __
       ss[r] += v[r][g].x * v[r][g].x + v[r][g].y * v[r][g].y + v[r][g].z * v[r][g].z + v[r][g].w * v[r][g].w;
 #pragma unroll
   for (int r = 0; r < 2; ++r) ss[r] = rownorm_warp_sum(ss[r]);
-  const float4* wr = reinterpret_cast<const float4*>(w);
   bool clip = false;
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -152,10 +157,9 @@ __global__ void rmsnorm768x2_kernel(const float* __restrict__ x, const float* __
     uint2* yr = reinterpret_cast<uint2*>(y + static_cast<size_t>(m0 + r) * D);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float4 ww = wr[lane + 32 * g];
       uint2 o;
-      o.x = pack_f16x2_sat(v[r][g].x * inv * ww.x, v[r][g].y * inv * ww.y, clip);
-      o.y = pack_f16x2_sat(v[r][g].z * inv * ww.z, v[r][g].w * inv * ww.w, clip);
+      o.x = pack_f16x2_sat(v[r][g].x * inv * ww[g].x, v[r][g].y * inv * ww[g].y, clip);
+      o.y = pack_f16x2_sat(v[r][g].z * inv * ww[g].z, v[r][g].w * inv * ww[g].w, clip);
       yr[lane + 32 * g] = o;
     }
   }
