@@ -104,13 +104,16 @@ __global__ void embed_rmsnorm_kernel(const uint8_t* __restrict__ table, const ui
 // norm of the updated row.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                __half* __restrict__ y, int M, int D, float eps, uint32_t* __restrict__ status) {
-  pdl_wait();
-  pdl_launch_next();  // after the wait: at most one grid waits ahead
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  // the norm weights are not written by the previous kernel: load them
+  // before waiting for it
+  const RowNormW ww = rownorm_load_w(w, D, lane);
+  pdl_wait();
+  pdl_launch_next();  // after the wait: at most one grid waits ahead
   if (m >= M) return;
   const bool clip = rownorm_row(x + static_cast<size_t>(m) * D, delta ? delta + static_cast<size_t>(m) * D : nullptr,
-                                true, w, y + static_cast<size_t>(m) * D, D, eps, lane);
+                                true, ww, y + static_cast<size_t>(m) * D, D, eps, lane);
   report_f16_clip(clip, status);
 }
 

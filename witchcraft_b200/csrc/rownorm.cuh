@@ -17,8 +17,22 @@ __device__ __forceinline__ float rownorm_warp_sum(float v) {
 // Lane owns float4 groups lane + 32 g, g < D / 128.  v = x (+ delta), written
 // back to x when write_x; y = f16(v * (1 / sqrt(mean(v^2) + eps)) * w).  y may
 // point to global or shared memory (8-byte aligned row).
+// The lane's norm weights (float4 groups lane + 32 g), loaded ahead of the
+// row so a kernel can issue them before it waits for its predecessor.
+struct RowNormW {
+  float4 v[kRowNormMaxD / 128];
+};
+__device__ __forceinline__ RowNormW rownorm_load_w(const float* __restrict__ w, int D, int lane) {
+  RowNormW r;
+  const float4* wr = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int g = 0; g < kRowNormMaxD / 128; ++g)
+    r.v[g] = g < D / 128 ? wr[lane + 32 * g] : make_float4(0.f, 0.f, 0.f, 0.f);
+  return r;
+}
+
 __device__ __forceinline__ bool rownorm_row(float* __restrict__ x, const float* __restrict__ delta, bool write_x,
-                                            const float* __restrict__ w, __half* __restrict__ y, int D, float eps,
+                                            const RowNormW& ww, __half* __restrict__ y, int D, float eps,
                                             int lane) {
   const int ng = D / 128;
   float4* xr = reinterpret_cast<float4*>(x);
@@ -45,19 +59,23 @@ __device__ __forceinline__ bool rownorm_row(float* __restrict__ x, const float* 
   // element (the product differs from the quotient by at most one f32 ulp)
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
   uint2* yr = reinterpret_cast<uint2*>(y);
-  const float4* wr = reinterpret_cast<const float4*>(w);
   bool clip = false;
 #pragma unroll
   for (int g = 0; g < kRowNormMaxD / 128; ++g) {
     if (g < ng) {
-      const float4 ww = wr[lane + 32 * g];
+      const float4 wg = ww.v[g];
       uint2 o;
-      o.x = pack_f16x2_sat(v[g].x * inv * ww.x, v[g].y * inv * ww.y, clip);
-      o.y = pack_f16x2_sat(v[g].z * inv * ww.z, v[g].w * inv * ww.w, clip);
+      o.x = pack_f16x2_sat(v[g].x * inv * wg.x, v[g].y * inv * wg.y, clip);
+      o.y = pack_f16x2_sat(v[g].z * inv * wg.z, v[g].w * inv * wg.w, clip);
       yr[lane + 32 * g] = o;
     }
   }
   return clip;  // whether an output value was clipped to the f16 range
+}
+__device__ __forceinline__ bool rownorm_row(float* __restrict__ x, const float* __restrict__ delta, bool write_x,
+                                            const float* __restrict__ w, __half* __restrict__ y, int D, float eps,
+                                            int lane) {
+  return rownorm_row(x, delta, write_x, rownorm_load_w(w, D, lane), y, D, eps, lane);
 }
 
 }  // namespace wc
